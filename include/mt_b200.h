@@ -1,0 +1,177 @@
+/*
+ * mt_b200.h -- C ABI of the B200 (sm_100a) transformer-op hot path.
+ *
+ * Every entry point takes plain device pointers, element counts, element
+ * strides and a cudaStream_t (passed as void*), launches its kernels on that
+ * stream and returns an mt_status code.  No entry point allocates device
+ * memory: scratch buffers ("workspace") are passed in by the caller, whose
+ * size is given by the matching *_workspace_bytes function.
+ *
+ * Each entry point names the reference operator it replaces
+ * (duoan/mega-trading, paths relative to the project root).  The reference
+ * binds those operators as Python functions; the Python mirror in
+ * mega_trading_b200/kernels/ keeps their names, signatures and errors and
+ * calls these functions through ctypes.
+ *
+ * dtype codes: MT_F32 = 0, MT_F16 = 1, MT_BF16 = 2.
+ */
+#ifndef MT_B200_H
+#define MT_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MT_API __attribute__((visibility("default")))
+#else
+#define MT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mt_dtype { MT_F32 = 0, MT_F16 = 1, MT_BF16 = 2 };
+
+enum mt_status {
+  MT_OK = 0,
+  MT_ERR_INVALID_ARGUMENT = 1,   /* shape / size / pointer mismatch            */
+  MT_ERR_UNSUPPORTED_DTYPE = 2,  /* dtype combination not implemented          */
+  MT_ERR_UNSUPPORTED_LAYOUT = 3, /* stride or alignment the kernel cannot take */
+  MT_ERR_UNSUPPORTED_ARCH = 4,   /* device is not sm_100                       */
+  MT_ERR_LAUNCH = 5,             /* CUDA launch / runtime error                */
+  MT_ERR_DEVICE_TIMEOUT = 6,     /* a bounded device-side wait gave up         */
+  MT_ERR_WORKSPACE = 7,          /* workspace pointer null or too small        */
+  MT_ERR_TENSOR_MAP = 8          /* cuTensorMapEncodeTiled rejected a layout   */
+};
+
+/* Human-readable text for a status code (static storage). */
+MT_API const char* mt_status_string(int status);
+
+/* Library version, and the compute capability the library was built for (100). */
+MT_API int mt_version(void);
+MT_API int mt_built_arch(void);
+
+/* Last CUDA error text seen by the library on this host thread (static storage). */
+MT_API const char* mt_last_error(void);
+
+/*
+ * Device status word.  The tcgen05 kernels take a pointer to one uint32 in
+ * device memory (caller-owned, zero-initialised).  A bounded wait that gives
+ * up writes a nonzero code there and the kernel returns early instead of
+ * hanging.  The host reads it back with an ordinary copy.
+ *   bit layout: (kernel_id << 16) | wait_site
+ */
+
+/* ---------------------------------------------------------------------
+ * RMSNorm   replaces triton_rms_norm (src/mega_trading/kernels/triton_ops.py:11-15,
+ *           forward kernel :528-538, backward :633-665 + torch sum :183)
+ *   y[r, :] = x[r, :] * rstd[r] * w,   rstd[r] = rsqrt(mean(x[r, :]^2) + eps)
+ * x, y: [rows, dim] contiguous; w: [dim]; rstd: [rows] fp32 (output).
+ * Math in fp32 for every dtype.
+ * ------------------------------------------------------------------- */
+MT_API int mt_rms_norm_fwd(const void* x, int x_dtype, const void* w, int w_dtype,
+                    void* y, int y_dtype, float* rstd, int64_t rows,
+                    int64_t dim, float eps, void* stream);
+
+/* Workspace (bytes) for mt_rms_norm_bwd / mt_add_rms_norm_bwd: fp32 per-block
+ * partial sums of dW. */
+MT_API int64_t mt_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t dim);
+
+/* dx = rstd * (dy*w - x * rstd^2 * mean(dy*w*x));  dw = sum_rows dy * x * rstd.
+ * dx: [rows, dim] in dx_dtype; dw: [dim] in dw_dtype (fully written, not
+ * accumulated). */
+MT_API int mt_rms_norm_bwd(const void* x, int x_dtype, const void* w, int w_dtype,
+                    const float* rstd, const void* dy, int dy_dtype, void* dx,
+                    int dx_dtype, void* dw, int dw_dtype, void* workspace,
+                    int64_t workspace_bytes, int64_t rows, int64_t dim,
+                    void* stream);
+
+/* ---------------------------------------------------------------------
+ * Fused residual add + RMSNorm   replaces triton_add_rms_norm
+ *   (src/mega_trading/kernels/triton_ops.py:18-42, forward kernel :541-566,
+ *    backward kernel :569-608 + torch sum :287)
+ *   new_residual = hidden + residual;  normed = RMSNorm(new_residual)
+ * All activations share one dtype (act_dtype); w has w_dtype.
+ * ------------------------------------------------------------------- */
+MT_API int mt_add_rms_norm_fwd(const void* hidden, const void* residual, int act_dtype,
+                        const void* w, int w_dtype, void* new_residual,
+                        int res_dtype, void* normed, int normed_dtype,
+                        float* rstd, int64_t rows, int64_t dim, float eps,
+                        void* stream);
+
+/* grad_input = grad_new_residual + dNorm(grad_normed);  the reference returns
+ * the same tensor for hidden and residual (triton_ops.py:291). */
+MT_API int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w,
+                        int w_dtype, const float* rstd,
+                        const void* grad_new_residual, int gres_dtype,
+                        const void* grad_normed, int gnorm_dtype,
+                        void* grad_input, int gin_dtype, void* dw, int dw_dtype,
+                        void* workspace, int64_t workspace_bytes, int64_t rows,
+                        int64_t dim, void* stream);
+
+/* ---------------------------------------------------------------------
+ * RoPE (interleaved pairs)   replaces triton_apply_rope
+ *   (src/mega_trading/kernels/triton_ops.py:45-54, _launch_rope_kernel
+ *    :477-525, _rope_kernel :690-761)
+ *   out[2i]   = x[2i]*cos[t,i] - x[2i+1]*sin[t,i]
+ *   out[2i+1] = x[2i]*sin[t,i] + x[2i+1]*cos[t,i]
+ * Backward is the same call with negate_sin = 1.
+ * q: [B, Hq, T, D], k: [B, Hk, T, D] with arbitrary element strides
+ * (qs[4], ks[4], qos[4], kos[4] = strides of q, k, q_out, k_out in elements);
+ * cos/sin: [T, D/2] with strides cs[2], ss[2].  One dtype for all tensors.
+ * ------------------------------------------------------------------- */
+MT_API int mt_rope(const void* q, const void* k, const void* cos, const void* sin,
+            void* q_out, void* k_out, int dtype, int64_t B, int64_t Hq,
+            int64_t Hk, int64_t T, int64_t D, const int64_t* qs,
+            const int64_t* ks, const int64_t* qos, const int64_t* kos,
+            const int64_t* cs, const int64_t* ss, int negate_sin, void* stream);
+
+/* ---------------------------------------------------------------------
+ * SwiGLU gate   replaces triton_swiglu_gate
+ *   (src/mega_trading/kernels/triton_ops.py:57-61, forward :774-782,
+ *    backward :799-819)
+ *   y = silu(g) * u, silu evaluated in fp32 and rounded to u's dtype first.
+ * g, u, y: n contiguous elements.
+ * ------------------------------------------------------------------- */
+MT_API int mt_swiglu_fwd(const void* g, const void* u, void* y, int dtype, int64_t n,
+                  void* stream);
+MT_API int mt_swiglu_bwd(const void* g, const void* u, const void* dy, void* dg,
+                  void* du, int dtype, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------
+ * Causal GQA flash attention (tcgen05 + TMEM + TMA)   replaces triton_attention
+ *   (src/mega_trading/kernels/triton_attention.py:12-24, forward :27-78 and
+ *    kernels :260-478, backward :80-111 and :134-245, :481-747)
+ * q/o: [B, Hq, T, D], k/v: [B, Hkv, T, D], Hq = Hkv * repeats, element
+ * strides qs[4] etc. (innermost stride must be 1, other strides multiples of
+ * 8 elements), D in {32, 64}, dtype bf16 or fp16.
+ * lse: [B, Hq, T] fp32 contiguous (natural-log logsumexp of scaled scores).
+ * scale: softmax scale (1/sqrt(D) in the reference).
+ * status: device uint32 (see above).
+ * ------------------------------------------------------------------- */
+MT_API int mt_attention_fwd(const void* q, const void* k, const void* v, void* o,
+                     float* lse, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                     int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
+                     const int64_t* vs, const int64_t* os, float scale,
+                     uint32_t* status, void* stream);
+
+/* Workspace for the backward: fp32 delta [B*Hq*Tp] and fp32 dQ accumulator
+ * [B*Hq*Tp*D], Tp = T rounded up to 128. */
+MT_API int64_t mt_attention_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t T,
+                                         int64_t D);
+
+MT_API int mt_attention_bwd(const void* q, const void* k, const void* v,
+                     const void* o, const float* lse, const void* dout,
+                     void* dq, void* dk, void* dv, int dtype, int64_t B,
+                     int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                     const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                     const int64_t* os, const int64_t* dos, const int64_t* dqs,
+                     const int64_t* dks, const int64_t* dvs, float scale,
+                     void* workspace, int64_t workspace_bytes, uint32_t* status,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MT_B200_H */

@@ -1,0 +1,163 @@
+"""ctypes binding of the C ABI in ``include/mt_b200.h`` (``lib/libmtb200.so``).
+
+The product path has no fallback: if the library is missing or the device is
+not an sm_100 GPU, the ops raise instead of silently running something else.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmtb200.so"
+
+MT_F32, MT_F16, MT_BF16 = 0, 1, 2
+_DTYPE_CODE = {torch.float32: MT_F32, torch.float16: MT_F16, torch.bfloat16: MT_BF16}
+
+c_i64 = ctypes.c_int64
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_vp = ctypes.c_void_p
+c_i64p = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes); mirrors include/mt_b200.h
+PROTOTYPES: dict[str, tuple[object, list[object]]] = {
+    "mt_status_string": (ctypes.c_char_p, [c_int]),
+    "mt_version": (c_int, []),
+    "mt_built_arch": (c_int, []),
+    "mt_last_error": (ctypes.c_char_p, []),
+    "mt_rms_norm_fwd": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64, c_float, c_vp]),
+    "mt_rms_norm_bwd_workspace_bytes": (c_i64, [c_i64, c_i64]),
+    "mt_rms_norm_bwd": (
+        c_int,
+        [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp],
+    ),
+    "mt_add_rms_norm_fwd": (
+        c_int,
+        [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64, c_float, c_vp],
+    ),
+    "mt_add_rms_norm_bwd": (
+        c_int,
+        [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64,
+         c_i64, c_vp],
+    ),
+    "mt_rope": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p,
+         c_i64p, c_i64p, c_i64p, c_int, c_vp],
+    ),
+    "mt_swiglu_fwd": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_vp]),
+    "mt_swiglu_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp]),
+    "mt_attention_fwd": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p, c_i64p,
+         c_float, c_vp, c_vp],
+    ),
+    "mt_attention_bwd_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
+    "mt_attention_bwd": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p,
+         c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_float, c_vp, c_i64, c_vp, c_vp],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class B200KernelError(RuntimeError):
+    """A C-ABI call returned a nonzero mt_status."""
+
+
+def load(path: Path | str | None = None) -> ctypes.CDLL:
+    """Load ``libmtb200.so`` once and attach the prototypes; raise if absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"B200 kernel library not found at {p}; build it with `python -m mega_trading_b200.build` "
+                "(there is no fallback implementation)"
+            )
+        lib = ctypes.CDLL(os.fspath(p))
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(lib, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(status: int, name: str) -> None:
+    if status != 0:
+        lib = load()
+        text = lib.mt_status_string(status).decode()
+        detail = lib.mt_last_error().decode()
+        raise B200KernelError(f"{name} failed: {text} (status {status}){': ' + detail if detail else ''}")
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[t]
+    except KeyError as exc:
+        raise RuntimeError(f"unsupported dtype {t}") from exc
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def i64_array(values) -> ctypes.Array:
+    arr = (ctypes.c_int64 * len(values))(*[int(v) for v in values])
+    return arr
+
+
+# Per-device uint32 status word for the bounded device waits.
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def read_status(device: torch.device) -> int:
+    """Return and clear the device status word (synchronises the device)."""
+    t = status_word(device)
+    v = int(t.item())
+    if v:
+        t.zero_()
+    return v
+
+
+def require_cuda_sm100(t: torch.Tensor, op: str) -> None:
+    if t.device.type != "cuda":
+        raise RuntimeError(f"{op} requires CUDA tensors (the B200 path has no CPU fallback)")
+    major, minor = torch.cuda.get_device_capability(t.device)
+    if major != 10 or minor != 0:
+        raise RuntimeError(f"{op} requires an sm_100 (B200) GPU, found sm_{major}{minor}")
+
+
+# Launch counter: every successful C-ABI compute call increments it by the
+# number of kernels it launched (used by bench.py to report gpu_launches).
+launches = 0
+
+
+def count(n: int) -> None:
+    global launches
+    launches += n

@@ -1,0 +1,622 @@
+// Causal grouped-query flash attention, backward, for sm_100a.
+//
+// Reference semantics (duoan/mega-trading):
+//   src/mega_trading/kernels/triton_attention.py:80-111 (torch backward for
+//   every shape: P from the saved scores, dS = P * (dP - rowsum(dP * P)),
+//   dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO, GQA grads summed over
+//   the query heads of a group), :134-245 and :481-747 (Triton server-shape
+//   backward: P recomputed from the saved logsumexp, Delta = rowsum(O * dO)).
+//
+// B200 design
+//   * preprocess kernel: Delta = rowsum(O * dO) and lse * log2(e) into padded
+//     fp32 workspace rows (+inf past T so padded queries get P = 0); the fp32
+//     dQ accumulator is zeroed with cudaMemsetAsync.
+//   * main kernel: one CTA = one 128-key tile of one (batch, KV head).  It
+//     loops over every query head of the GQA group and every causal query
+//     tile (query tile >= key tile).  All five products are tcgen05.mma with
+//     fp32 accumulators in TMEM:
+//         S^T  = K Q^T        cols [0,128)        (M=128 keys, N=128 queries)
+//         dP^T = V dO^T       cols [128,256)
+//         dV  += P^T dO       cols [256,256+D)    (accumulated over the group)
+//         dK  += dS^T Q       cols [256+D,256+2D)
+//         dQ   = dS K         cols [256+2D,256+3D) (M=128 queries)
+//     P^T and dS^T are written once, bf16/fp16, to 128B-swizzled shared
+//     tiles; dS^T serves as the K-major A operand of dK and, read MN-major,
+//     as the A operand of dQ.  Q, dO and K are consumed MN-major where they
+//     act as B of a key-contracted product, so nothing is transposed.
+//   * dQ partials leave the CTA through a TMA bulk tensor reduce-add (fp32)
+//     from a 128B-swizzled staging tile; dK/dV never leave TMEM until the
+//     group is done (no atomics for them).
+//   * Warp roles: warps 0-7 = two compute warpgroups (thread = key row for
+//     S/dP/dS, = query row for the dQ drain; the two groups split the query
+//     columns), warp 8 = TMA producer (+ TMEM allocation), warp 9 = MMA.
+//   * postprocess kernel: dQ = bf16(scale * dQacc) in the caller's layout.
+//   * Every mbarrier wait is bounded (status word + early exit, no trap).
+#include <cmath>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace mt {
+
+int make_bhtd_map(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                  const int64_t* s, int box_rows, int* swapped);
+int check_attn_layout(const void* ptr, const int64_t* s, bool need);
+
+namespace {
+
+constexpr int kBK = 128;  // keys per CTA
+constexpr int kBQ = 128;  // queries per tile
+constexpr int kNQ = 2;    // Q/dO pipeline stages
+constexpr int kThreads = 320;
+constexpr uint32_t kKernelId = 2;
+
+template <int D>
+struct BwdCfg {
+  static constexpr int ROW_BYTES = D * 2;
+  static constexpr uint32_t LAYOUT = (D == 64) ? kSwizzle128 : kSwizzle64;
+  static constexpr int SBO = 8 * ROW_BYTES;
+  static constexpr int TILE = 128 * ROW_BYTES;
+  static constexpr int PT_BYTES = kBK * kBQ * 2;  // one P^T or dS^T tile
+  static constexpr int DQ_BYTES = kBQ * D * 4;    // fp32 dQ staging (D/32 boxes of 16 KB)
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE;
+  static constexpr int OFF_Q = OFF_V + TILE;
+  static constexpr int OFF_DO = OFF_Q + kNQ * TILE;
+  static constexpr int OFF_P = OFF_DO + kNQ * TILE;
+  static constexpr int OFF_DS = OFF_P + PT_BYTES;
+  static constexpr int OFF_DQ = OFF_DS + PT_BYTES;
+  static constexpr int OFF_LSE = OFF_DQ + DQ_BYTES;      // [kNQ][128] fp32
+  static constexpr int OFF_DELTA = OFF_LSE + kNQ * 512;  // [kNQ][128] fp32
+  static constexpr int OFF_BAR = OFF_DELTA + kNQ * 512;
+  static constexpr int SMEM = OFF_BAR + 256;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D, T_DQ = 256 + 2 * D;
+};
+
+struct BwdParams {
+  CUtensorMap tm_q, tm_k, tm_v, tm_do, tm_dq;  // tm_dq: fp32 accumulator [rows, D]
+  int sw_q, sw_k, sw_v, sw_do;                 // coordinate order of each bf16 map
+  const float* lse2;                           // [B*Hq*Tp] lse * log2(e), +inf past T
+  const float* delta;                          // [B*Hq*Tp]
+  void* dk;
+  void* dv;
+  int64_t dks[4], dvs[4];
+  int T, Tp, Hq, Hkv, repeats, n_tiles;
+  float scale_log2, scale;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, uint64_t* bar, int t0, int h, int b,
+                                         int swapped) {
+  if (swapped)
+    tma_load_4d(dst, map, bar, 0, h, t0, b);
+  else
+    tma_load_4d(dst, map, bar, 0, t0, h, b);
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Write 32 consecutive query columns (col0 .. col0+31, col0 % 32 == 0) of one
+// key row into a 128B-swizzled [128 rows][64 cols] x 2 K-major tile.
+template <typename T>
+__device__ __forceinline__ void store_row32(uint8_t* tile, int row, int col0, const float (&v)[32]) {
+  uint8_t* base = tile + (col0 >> 6) * (128 * 128) + row * 128;
+  const int ch0 = (col0 & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack2<T>(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack2<T>(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack2<T>(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack2<T>(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(base + (((ch0 + q) ^ (row & 7)) * 16)) = w;
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_constant__ BwdParams p) {
+  using C = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0u, (kKernelId << 16) | 0xFFFFu);
+    return;
+  }
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sDO = smem + C::OFF_DO;
+  uint8_t* sP = smem + C::OFF_P;
+  uint8_t* sDS = smem + C::OFF_DS;
+  uint8_t* sDQ = smem + C::OFF_DQ;
+  float* sLse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* sDelta = reinterpret_cast<float*>(smem + C::OFF_DELTA);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* bar_kv = bars + 0;
+  uint64_t* bar_q_full = bars + 1;           // [kNQ]
+  uint64_t* bar_q_empty = bar_q_full + kNQ;  // [kNQ]
+  uint64_t* bar_sd_full = bar_q_empty + kNQ;
+  uint64_t* bar_sd_free = bar_sd_full + 1;
+  uint64_t* bar_pds_full = bar_sd_full + 2;
+  uint64_t* bar_dq_full = bar_sd_full + 3;
+  uint64_t* bar_dq_free = bar_sd_full + 4;
+  uint64_t* bar_done = bar_sd_full + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+
+  const int bk = blockIdx.x;
+  const int b = bk / p.Hkv;
+  const int hk = bk - b * p.Hkv;
+  const int kt = (int)blockIdx.y;  // heaviest (smallest) key tiles launch first
+  const int n_q = p.n_tiles - kt;  // causal query tiles per head: kt .. n_tiles-1
+  const int n_it = n_q * p.repeats;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_kv, 1);
+    for (int s = 0; s < kNQ; ++s) {
+      mbar_init(&bar_q_full[s], 1);
+      mbar_init(&bar_q_empty[s], 1);
+    }
+    mbar_init(bar_sd_full, 1);
+    mbar_init(bar_sd_free, 256);
+    mbar_init(bar_pds_full, 256);
+    mbar_init(bar_dq_full, 1);
+    mbar_init(bar_dq_free, 256);
+    mbar_init(bar_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx wc{p.status, abort_flag, kKernelId};
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_q);
+      tma_prefetch_desc(&p.tm_k);
+      tma_prefetch_desc(&p.tm_v);
+      tma_prefetch_desc(&p.tm_do);
+      mbar_arrive_expect_tx(bar_kv, 2 * C::TILE);
+      tma_tile(sK, &p.tm_k, bar_kv, kt * kBK, hk, b, p.sw_k);
+      tma_tile(sV, &p.tm_v, bar_kv, kt * kBK, hk, b, p.sw_v);
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it % kNQ;
+        const int r = it / n_q;
+        const int qi = kt + (it - r * n_q);
+        const int h = hk * p.repeats + r;
+        if (it >= kNQ && !wait_bounded(wc, &bar_q_empty[st], ((it / kNQ) & 1) ^ 1, 1)) break;
+        mbar_arrive_expect_tx(&bar_q_full[st], 2 * C::TILE + 2 * 512);
+        tma_tile(sQ + st * C::TILE, &p.tm_q, &bar_q_full[st], qi * kBQ, h, b, p.sw_q);
+        tma_tile(sDO + st * C::TILE, &p.tm_do, &bar_q_full[st], qi * kBQ, h, b, p.sw_do);
+        const int64_t row0 = (int64_t(b) * p.Hq + h) * p.Tp + int64_t(qi) * kBQ;
+        bulk_load(sLse + st * 128, p.lse2 + row0, 512, &bar_q_full[st]);
+        bulk_load(sDelta + st * 128, p.delta + row0, 512, &bar_q_full[st]);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // copies already issued must land before shared memory is released
+        wait_drain(wc, bar_kv, 0, 11);
+        for (int it = (issued > kNQ ? issued - kNQ : 0); it < issued; ++it)
+          wait_drain(wc, &bar_q_full[it % kNQ], (it / kNQ) & 1, 12);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t idesc_sd = make_idesc(128, kBQ, kBf16, 0, 0);  // K-major A and B
+      constexpr uint32_t idesc_acc = make_idesc(128, D, kBf16, 0, 1);   // A K-major, B MN-major
+      constexpr uint32_t idesc_dq = make_idesc(128, D, kBf16, 1, 1);    // A and B MN-major
+      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
+      const uint32_t p_base = smem_u32(sP), ds_base = smem_u32(sDS);
+      bool ok = wait_bounded(wc, bar_kv, 0, 2);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % kNQ;
+        if (!wait_bounded(wc, &bar_q_full[st], (it / kNQ) & 1, 3) ||
+            (it > 0 && !wait_bounded(wc, bar_sd_free, (it - 1) & 1, 4))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_ss(tmem + C::T_S, make_sdesc(k_base + kk * 32, 16, C::SBO, C::LAYOUT),
+                  make_sdesc(qb + kk * 32, 16, C::SBO, C::LAYOUT), idesc_sd, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_ss(tmem + C::T_DP, make_sdesc(v_base + kk * 32, 16, C::SBO, C::LAYOUT),
+                  make_sdesc(dob + kk * 32, 16, C::SBO, C::LAYOUT), idesc_sd, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_sd_full);
+        if (!wait_bounded(wc, bar_pds_full, it & 1, 5)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
+#pragma unroll
+        for (int kk = 0; kk < kBQ / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          const uint32_t b_off = kk * 16 * C::ROW_BYTES;
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          umma_ss(tmem + C::T_DV, make_sdesc(p_base + a_off, 16, 1024, kSwizzle128),
+                  make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
+          umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
+                  make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
+        }
+        if (it > 0 && !wait_bounded(wc, bar_dq_free, (it - 1) & 1, 6)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // dQ = dS K   (M = 128 queries, K = 128 keys in steps of 16)
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          umma_ss(tmem + C::T_DQ, make_sdesc(ds_base + kk * 2048, 128 * 128, 1024, kSwizzle128),
+                  make_sdesc(k_base + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT), idesc_dq,
+                  kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_dq_full);
+        umma_commit(&bar_q_empty[st]);
+      }
+      // every issued MMA completes before TMEM is released (also on abort)
+      umma_commit(bar_done);
+      if (!ok) wait_drain(wc, bar_done, 0, 13);
+    }
+  } else {
+    // ------------------------------------------------------------ compute
+    const int wg = warp >> 2;          // query-column half handled by this warpgroup
+    const int r = threadIdx.x & 127;   // TMEM lane: key row (S/dP) or query row (dQ)
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const int key = kt * kBK + r;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int st = it % kNQ;
+      const int rr = it / n_q;
+      const int qi = kt + (it - rr * n_q);
+      const int h = hk * p.repeats + rr;
+      const bool diag = (qi == kt);
+      if (!bar_all(wait_bounded(wc, bar_sd_full, it & 1, 8), 4, 256)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lse = sLse + st * 128;
+      const float* dl = sDelta + st * 128;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = wg * 64 + c * 32;
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lane_off + C::T_S + col0, sv);
+        tmem_ld32(tmem + lane_off + C::T_DP + col0, dv);
+        tmem_ld_wait();
+        float pv[32], dsv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int q = qi * kBQ + col0 + i;
+          float pp = fast_exp2(__uint_as_float(sv[i]) * p.scale_log2 - lse[col0 + i]);
+          if (diag && key > q) pp = 0.f;
+          pv[i] = pp;
+          dsv[i] = pp * (__uint_as_float(dv[i]) - dl[col0 + i]);
+        }
+        store_row32<T>(sP, r, col0, pv);
+        store_row32<T>(sDS, r, col0, dsv);
+      }
+      tc_fence_before();
+      mbar_arrive(bar_sd_free);
+      fence_proxy_async_smem();
+      mbar_arrive(bar_pds_full);
+
+      // drain dQ of this tile: TMEM -> swizzled fp32 staging -> TMA reduce-add
+      if (!bar_all(wait_bounded(wc, bar_dq_full, it & 1, 9), 4, 256)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      constexpr int kCols = D / 2;  // dQ columns per warpgroup
+      uint32_t qv[kCols];
+      if constexpr (kCols == 32) {
+        tmem_ld32(tmem + lane_off + C::T_DQ + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(qv));
+      } else {
+        tmem_ld16(tmem + lane_off + C::T_DQ + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(qv));
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(bar_dq_free);
+      const bool leader = (threadIdx.x & 127) == 0;
+      // the previous reduce of this warpgroup must have finished reading staging
+      if (leader) bulk_wait_group_read0();
+      named_bar_sync(1 + wg, 128);
+      {
+        // fp32 staging: box bx = 32 columns x 128 rows, 128 B rows, 128B swizzle
+        const int colbase = wg * kCols;
+#pragma unroll
+        for (int q = 0; q < kCols / 4; ++q) {
+          const int col = colbase + q * 4;
+          const int bx = col >> 5;
+          const int ch = (col & 31) >> 2;
+          uint4 w;
+          w.x = qv[q * 4 + 0];
+          w.y = qv[q * 4 + 1];
+          w.z = qv[q * 4 + 2];
+          w.w = qv[q * 4 + 3];
+          *reinterpret_cast<uint4*>(sDQ + bx * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16)) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1 + wg, 128);
+      if (leader) {
+        const int row0 = (b * p.Hq + h) * p.Tp + qi * kBQ;
+        if constexpr (kCols == 32) {
+          tma_reduce_add_2d(&p.tm_dq, sDQ + wg * (128 * 128), wg * 32, row0);
+          bulk_commit_group();
+        } else if (wg == 1) {
+          // D == 32: both halves live in box 0; warpgroup 1 issues after both wrote
+        }
+      }
+      if constexpr (kCols != 32) {
+        named_bar_sync(3, 256);
+        if (threadIdx.x == 0) {
+          tma_reduce_add_2d(&p.tm_dq, sDQ, 0, (b * p.Hq + h) * p.Tp + qi * kBQ);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+        }
+        named_bar_sync(3, 256);
+      }
+    }
+    // final: dV and dK (scaled) for this key tile
+    if (ok && bar_all(wait_bounded(wc, bar_done, 0, 10), 4, 256)) {
+      tc_fence_after();
+      constexpr int kCols = D / 2;
+      uint32_t vv[kCols], kv[kCols];
+      if constexpr (kCols == 32) {
+        tmem_ld32(tmem + lane_off + C::T_DV + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(vv));
+        tmem_ld32(tmem + lane_off + C::T_DK + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(kv));
+      } else {
+        tmem_ld16(tmem + lane_off + C::T_DV + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(vv));
+        tmem_ld16(tmem + lane_off + C::T_DK + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(kv));
+      }
+      tmem_ld_wait();
+      if (key < p.T) {
+        T* dvrow = static_cast<T*>(p.dv) + int64_t(b) * p.dvs[0] + int64_t(hk) * p.dvs[1] + int64_t(key) * p.dvs[2] +
+                   wg * kCols;
+        T* dkrow = static_cast<T*>(p.dk) + int64_t(b) * p.dks[0] + int64_t(hk) * p.dks[1] + int64_t(key) * p.dks[2] +
+                   wg * kCols;
+#pragma unroll
+        for (int q = 0; q < kCols / 8; ++q) {
+          uint4 a, c;
+          a.x = pack2<T>(__uint_as_float(vv[q * 8 + 0]), __uint_as_float(vv[q * 8 + 1]));
+          a.y = pack2<T>(__uint_as_float(vv[q * 8 + 2]), __uint_as_float(vv[q * 8 + 3]));
+          a.z = pack2<T>(__uint_as_float(vv[q * 8 + 4]), __uint_as_float(vv[q * 8 + 5]));
+          a.w = pack2<T>(__uint_as_float(vv[q * 8 + 6]), __uint_as_float(vv[q * 8 + 7]));
+          c.x = pack2<T>(__uint_as_float(kv[q * 8 + 0]) * p.scale, __uint_as_float(kv[q * 8 + 1]) * p.scale);
+          c.y = pack2<T>(__uint_as_float(kv[q * 8 + 2]) * p.scale, __uint_as_float(kv[q * 8 + 3]) * p.scale);
+          c.z = pack2<T>(__uint_as_float(kv[q * 8 + 4]) * p.scale, __uint_as_float(kv[q * 8 + 5]) * p.scale);
+          c.w = pack2<T>(__uint_as_float(kv[q * 8 + 6]) * p.scale, __uint_as_float(kv[q * 8 + 7]) * p.scale);
+          *reinterpret_cast<uint4*>(dvrow + q * 8) = a;
+          *reinterpret_cast<uint4*>(dkrow + q * 8) = c;
+        }
+      }
+    }
+    // outstanding dQ reductions must finish before the CTA's shared memory goes away
+    if ((threadIdx.x & 127) == 0) bulk_wait_group0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// preprocess: delta = rowsum(O * dO), lse2 = lse * log2(e) (+inf past T)
+// 8 (D=64) or 4 (D=32) lanes per row, 16-byte loads.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, const T* __restrict__ dout,
+                                                    const float* __restrict__ lse, float* __restrict__ delta,
+                                                    float* __restrict__ lse2, int64_t os0, int64_t os1, int64_t os2,
+                                                    int64_t ds0, int64_t ds1, int64_t ds2, int Hq, int seq, int Tp,
+                                                    int64_t rows) {
+  constexpr int LPR = D / 8;  // lanes per row
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gid / LPR;
+  const int sub = (int)(gid % LPR);
+  const bool valid_row = row < rows;
+  int64_t bh = valid_row ? row / Tp : 0;
+  const int t = valid_row ? (int)(row - bh * Tp) : 0;
+  const int b = (int)(bh / Hq), h = (int)(bh - int64_t(b) * Hq);
+  float acc = 0.f;
+  if (valid_row && t < seq) {
+    float a[8], c[8];
+    load_vec<T, 8>(o + b * os0 + h * os1 + int64_t(t) * os2 + sub * 8, a);
+    load_vec<T, 8>(dout + b * ds0 + h * ds1 + int64_t(t) * ds2 + sub * 8, c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fmaf(a[i], c[i], acc);
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (valid_row && sub == 0) {
+    delta[row] = acc;
+    lse2[row] = (t < seq) ? lse[bh * seq + t] * 1.4426950408889634f : INFINITY;
+  }
+}
+
+// postprocess: dq[b,h,t,:] = scale * dq_acc[row, :]
+template <typename T, int D>
+__global__ void __launch_bounds__(256) attn_bwd_post(const float* __restrict__ acc, T* __restrict__ dq,
+                                                     int64_t s0, int64_t s1, int64_t s2, int Hq, int seq, int Tp,
+                                                     float scale, int64_t rows) {
+  constexpr int LPR = D / 8;
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gid / LPR;
+  const int sub = (int)(gid % LPR);
+  if (row >= rows) return;
+  const int64_t bh = row / Tp;
+  const int t = (int)(row - bh * Tp);
+  if (t >= seq) return;
+  const int b = (int)(bh / Hq), h = (int)(bh - int64_t(b) * Hq);
+  const float4* src = reinterpret_cast<const float4*>(acc + row * D + sub * 8);
+  const float4 x = src[0], y = src[1];
+  const float v[8] = {x.x * scale, x.y * scale, x.z * scale, x.w * scale,
+                      y.x * scale, y.y * scale, y.z * scale, y.w * scale};
+  store_vec<T, 8>(dq + b * s0 + h * s1 + int64_t(t) * s2 + sub * 8, v);
+}
+
+struct Workspace {
+  float* delta;
+  float* lse2;
+  float* dq_acc;
+  int64_t bytes;
+};
+
+Workspace carve(void* base, int64_t B, int64_t Hq, int64_t T, int64_t D) {
+  const int64_t Tp = (T + 127) / 128 * 128;
+  const int64_t rows = B * Hq * Tp;
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  Workspace w;
+  char* p = static_cast<char*>(base);
+  const int64_t a = up(rows * 4), c = up(rows * D * 4);
+  w.delta = reinterpret_cast<float*>(p);
+  w.lse2 = reinterpret_cast<float*>(p + a);
+  w.dq_acc = reinterpret_cast<float*>(p + 2 * a);
+  w.bytes = 2 * a + c;
+  return w;
+}
+
+template <typename T, int D>
+int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, void* dq, const int64_t* os,
+            const int64_t* dos, const int64_t* dqs, Workspace& ws, int B, cudaStream_t stream) {
+  using C = BwdCfg<D>;
+  const int64_t rows = int64_t(B) * prm.Hq * prm.Tp;
+  cudaError_t e = cudaMemsetAsync(ws.dq_acc, 0, rows * D * 4, stream);
+  if (e != cudaSuccess) {
+    set_last_error("cudaMemsetAsync(dq_acc)", e);
+    return MT_ERR_LAUNCH;
+  }
+  {
+    const int64_t threads = rows * (D / 8);
+    attn_bwd_pre<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+        static_cast<const T*>(o), static_cast<const T*>(dout), lse, ws.delta, ws.lse2, os[0], os[1], os[2], dos[0],
+        dos[1], dos[2], prm.Hq, prm.T, prm.Tp, rows);
+    int st = check_launch("attention_bwd_pre");
+    if (st != MT_OK) return st;
+  }
+  {
+    auto kern = attn_bwd_kernel<T, D>;
+    int st = set_smem_limit((const void*)kern, C::SMEM);
+    if (st != MT_OK) return st;
+    dim3 grid((unsigned)(B * prm.Hkv), (unsigned)prm.n_tiles);
+    kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
+    st = check_launch("attention_bwd");
+    if (st != MT_OK) return st;
+  }
+  {
+    const int64_t threads = rows * (D / 8);
+    attn_bwd_post<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+        ws.dq_acc, static_cast<T*>(dq), dqs[0], dqs[1], dqs[2], prm.Hq, prm.T, prm.Tp, prm.scale, rows);
+    return check_launch("attention_bwd_post");
+  }
+}
+
+}  // namespace
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int64_t mt_attention_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t T, int64_t D) {
+  if (B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
+  return carve(nullptr, B, Hq, T, D).bytes;
+}
+
+extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                                const void* dout, void* dq, void* dk, void* dv, int dtype, int64_t B, int64_t Hq,
+                                int64_t Hkv, int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
+                                const int64_t* vs, const int64_t* os, const int64_t* dos, const int64_t* dqs,
+                                const int64_t* dks, const int64_t* dvs, float scale, void* workspace,
+                                int64_t workspace_bytes, uint32_t* status, void* stream) {
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || (Hq % Hkv) != 0) return MT_ERR_INVALID_ARGUMENT;
+  if (D != 64 && D != 32) return MT_ERR_INVALID_ARGUMENT;
+  if (B == 0 || T == 0) return MT_OK;
+  if (lse == nullptr || status == nullptr) return MT_ERR_INVALID_ARGUMENT;
+  const int64_t Tp = (T + 127) / 128 * 128;
+  if (B * Hq * Tp > 0x7fffffffLL || B * Hkv > 0x7fffffffLL) return MT_ERR_INVALID_ARGUMENT;
+  int st = MT_OK;
+  const void* ptrs[9] = {q, k, v, o, dout, dq, dk, dv, nullptr};
+  const int64_t* strides[8] = {qs, ks, vs, os, dos, dqs, dks, dvs};
+  for (int i = 0; i < 8; ++i)
+    if ((st = check_attn_layout(ptrs[i], strides[i], true)) != MT_OK) return st;
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MT_ERR_WORKSPACE;
+  Workspace ws = carve(workspace, B, Hq, T, D);
+  if (workspace_bytes < ws.bytes) return MT_ERR_WORKSPACE;
+  if ((st = check_arch()) != MT_OK) return st;
+
+  BwdParams prm;
+  // coordinate orders: q/k/v follow the forward's choice; dO gets its own
+  int swq = (Hq == 1 || T == 1) ? 0 : -1;
+  if ((st = make_bhtd_map(&prm.tm_q, q, dtype, B, Hq, T, D, qs, kBQ, &swq)) != MT_OK) return st;
+  int swk = (Hkv == 1 || T == 1) ? 0 : -1, swv = swk, swdo = (Hq == 1 || T == 1) ? 0 : -1;
+  if ((st = make_bhtd_map(&prm.tm_k, k, dtype, B, Hkv, T, D, ks, kBK, &swk)) != MT_OK) return st;
+  if ((st = make_bhtd_map(&prm.tm_v, v, dtype, B, Hkv, T, D, vs, kBK, &swv)) != MT_OK) return st;
+  if ((st = make_bhtd_map(&prm.tm_do, dout, dtype, B, Hq, T, D, dos, kBQ, &swdo)) != MT_OK) return st;
+  {
+    // fp32 dQ accumulator as a 2-D tensor [B*Hq*Tp rows, D] with 32-column boxes
+    uint64_t dims[2] = {(uint64_t)D, (uint64_t)(B * Hq * Tp)};
+    uint64_t strides_b[1] = {(uint64_t)(D * 4)};
+    uint32_t box[2] = {32, 128};
+    if ((st = encode_tensor_map(&prm.tm_dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ws.dq_acc, dims, strides_b, box,
+                                CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK)
+      return st;
+  }
+  prm.sw_q = swq;
+  prm.sw_k = swk;
+  prm.sw_v = swv;
+  prm.sw_do = swdo;
+  prm.lse2 = ws.lse2;
+  prm.delta = ws.delta;
+  prm.dk = dk;
+  prm.dv = dv;
+  for (int i = 0; i < 4; ++i) {
+    prm.dks[i] = dks[i];
+    prm.dvs[i] = dvs[i];
+  }
+  prm.T = (int)T;
+  prm.Tp = (int)Tp;
+  prm.Hq = (int)Hq;
+  prm.Hkv = (int)Hkv;
+  prm.repeats = (int)(Hq / Hkv);
+  prm.n_tiles = (int)(Tp / 128);
+  prm.scale = scale;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.status = status;
+  if (prm.n_tiles > 65535) return MT_ERR_INVALID_ARGUMENT;
+  auto s = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == MT_BF16;
+  const int b = (int)B;
+  if (D == 64)
+    return bf ? run_bwd<__nv_bfloat16, 64>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s)
+              : run_bwd<__half, 64>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s);
+  return bf ? run_bwd<__nv_bfloat16, 32>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s)
+            : run_bwd<__half, 32>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s);
+}

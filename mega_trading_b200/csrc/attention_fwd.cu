@@ -1,0 +1,476 @@
+// Causal grouped-query flash attention, forward, for sm_100a.
+//
+// Reference semantics (duoan/mega-trading):
+//   src/mega_trading/kernels/triton_attention.py:12-24 (validation), :27-78
+//   (forward: O and fp32 logsumexp saved for backward, scale = 1/sqrt(D)),
+//   :260-358 / :361-478 (online-softmax kernels).  Torch oracle:
+//   F.scaled_dot_product_attention(is_causal=True, enable_gqa=True)
+//   (model.py:228-235).
+//
+// B200 design
+//   * One CTA = two consecutive 128-row query tiles ("slots") of one
+//     (batch, query head); both slots share one K/V tile stream.  One CTA
+//     per SM (160 KB smem, all 512 TMEM columns).
+//   * Warp roles: warps 0-3 / 4-7 = softmax of slot 0 / 1 (thread i owns TMEM
+//     lane = query row i of its slot), warp 8 = TMA producer (+ TMEM
+//     allocation), warp 9 = tcgen05.mma issuer.
+//   * Per slot s: S = Q K^T (M=128, N=128, K=D) accumulates in TMEM columns
+//     [256s, 256s+128); O += P V (M=128, N=D, K=128) in [256s+128, 256s+128+D).
+//   * Q/K/V tiles arrive by TMA (no multicast) in the 128B (D=64) or 64B (D=32)
+//     swizzle that the UMMA shared-memory descriptors expect; V is consumed
+//     MN-major so it needs no transpose.  K/V are double-buffered.
+//   * P is rounded to the input dtype (as the reference does before its PV
+//     dot, triton_attention.py:340) and written to a 128B-swizzled K-major
+//     shared tile for the PV MMA.
+//   * Causal: key tiles 0..qtile only; the diagonal tile is masked in
+//     registers.  CTAs are launched heaviest query tile first.
+//   * Every mbarrier wait is bounded (status word + early exit, no trap).
+#include <cmath>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace mt {
+namespace {
+
+constexpr int kBM = 128;  // query rows per slot
+constexpr int kBN = 128;  // keys per tile
+constexpr int kSlots = 2;  // query tiles per CTA (consecutive tiles of one head)
+constexpr int kThreads = 320;
+constexpr uint32_t kKernelId = 1;
+
+template <int D>
+struct FwdCfg {
+  static constexpr int ROW_BYTES = D * 2;
+  static constexpr uint32_t LAYOUT = (D == 64) ? kSwizzle128 : kSwizzle64;
+  static constexpr int SBO = 8 * ROW_BYTES;  // bytes between 8-row core groups
+  static constexpr int TILE = kBM * ROW_BYTES;
+  static constexpr int NST = 2;
+  static constexpr int P_BYTES = kBM * kBN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + kSlots * TILE;
+  static constexpr int OFF_V = OFF_K + NST * TILE;
+  static constexpr int OFF_P = OFF_V + NST * TILE;
+  static constexpr int OFF_BAR = OFF_P + kSlots * P_BYTES;
+  static constexpr int SMEM = OFF_BAR + 512;
+  static constexpr int TMEM_COLS = 512;  // slot s: S at 256*s, O at 256*s + 128
+};
+
+struct FwdParams {
+  CUtensorMap tm_q, tm_k, tm_v;
+  void* o;
+  float* lse;
+  int64_t os[4];
+  int T, Hq, Hkv, repeats, n_qtiles, n_pairs;
+  int ht_swapped;  // tensor-map coordinate order (D, H, T, B) instead of (D, T, H, B)
+  float scale_log2;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, uint64_t* bar, int t0, int h, int b,
+                                         int swapped) {
+  if (swapped)
+    tma_load_4d(dst, map, bar, 0, h, t0, b);
+  else
+    tma_load_4d(dst, map, bar, 0, t0, h, b);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ FwdParams p) {
+  using C = FwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if ((smem_u32(smem) & 1023u) != 0) {  // swizzled tiles need 1 KB alignment
+    if (threadIdx.x == 0) atomicCAS(p.status, 0u, (kKernelId << 16) | 0xFFFFu);
+    return;
+  }
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sP = smem + C::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* bar_q = bars + 0;                    // [kSlots]
+  uint64_t* bar_k_full = bars + 2;               // [NST]
+  uint64_t* bar_v_full = bar_k_full + C::NST;    // [NST]
+  uint64_t* bar_kv_empty = bar_v_full + C::NST;  // [NST]
+  uint64_t* bar_s_full = bar_kv_empty + C::NST;  // [kSlots]
+  uint64_t* bar_s_free = bar_s_full + kSlots;    // [kSlots]
+  uint64_t* bar_p_full = bar_s_free + kSlots;    // [kSlots]
+  uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
+
+  const int bh = blockIdx.x;
+  const int b = bh / p.Hq;
+  const int h = bh - b * p.Hq;
+  const int hk = h / p.repeats;
+  const int pair = p.n_pairs - 1 - (int)blockIdx.y;  // heaviest pair first
+  // slot s handles query tile 2*pair + s; it sees key tiles 0..(2*pair + s)
+  const bool active1 = (2 * pair + 1) < p.n_qtiles;
+  const int nkv0 = 2 * pair + 1;
+  const int nkv1 = active1 ? 2 * pair + 2 : 0;
+  const int n_kv = active1 ? nkv1 : nkv0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bar_q[s], 1);
+      mbar_init(&bar_s_full[s], 1);
+      mbar_init(&bar_s_free[s], 128);
+      mbar_init(&bar_p_full[s], 128);
+      mbar_init(&bar_o_done[s], 1);
+    }
+    mbar_init(bar_o_done + kSlots, 1);  // final MMA drain
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&bar_k_full[s], 1);
+      mbar_init(&bar_v_full[s], 1);
+      mbar_init(&bar_kv_empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx wc{p.status, abort_flag, kKernelId};
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_q);
+      tma_prefetch_desc(&p.tm_k);
+      tma_prefetch_desc(&p.tm_v);
+      for (int s = 0; s < (active1 ? 2 : 1); ++s) {
+        mbar_arrive_expect_tx(&bar_q[s], C::TILE);
+        tma_tile(sQ + s * C::TILE, &p.tm_q, &bar_q[s], (2 * pair + s) * kBM, h, b, p.ht_swapped);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::NST;
+        if (j >= C::NST && !wait_bounded(wc, &bar_kv_empty[st], ((j / C::NST) & 1) ^ 1, 1)) break;
+        mbar_arrive_expect_tx(&bar_k_full[st], C::TILE);
+        tma_tile(sK + st * C::TILE, &p.tm_k, &bar_k_full[st], j * kBN, hk, b, p.ht_swapped);
+        mbar_arrive_expect_tx(&bar_v_full[st], C::TILE);
+        tma_tile(sV + st * C::TILE, &p.tm_v, &bar_v_full[st], j * kBN, hk, b, p.ht_swapped);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // copies already issued must land before shared memory is released
+        for (int s = 0; s < (active1 ? 2 : 1); ++s) wait_drain(wc, &bar_q[s], 0, 11);
+        for (int j = (issued > C::NST ? issued - C::NST : 0); j < issued; ++j) {
+          wait_drain(wc, &bar_k_full[j % C::NST], (j / C::NST) & 1, 12);
+          wait_drain(wc, &bar_v_full[j % C::NST], (j / C::NST) & 1, 12);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t idesc_s = make_idesc(kBM, kBN, kBf16, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc(kBM, D, kBf16, 0, 1);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t k_base = smem_u32(sK);
+      const uint32_t v_base = smem_u32(sV);
+      const uint32_t p_base = smem_u32(sP);
+      auto issue_s = [&](int slot, int st) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = make_sdesc(q_base + slot * C::TILE + kk * 32, 16, C::SBO, C::LAYOUT);
+          const uint64_t bd = make_sdesc(k_base + st * C::TILE + kk * 32, 16, C::SBO, C::LAYOUT);
+          umma_ss(tmem + slot * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int slot, int st, bool acc_first) {
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t ad = make_sdesc(p_base + slot * C::P_BYTES + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16,
+                                         1024, kSwizzle128);
+          const uint64_t bd = make_sdesc(v_base + st * C::TILE + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT);
+          umma_ss(tmem + slot * 256 + 128, ad, bd, idesc_o, (acc_first || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = wait_bounded(wc, &bar_q[0], 0, 2) && (!active1 || wait_bounded(wc, &bar_q[1], 0, 2)) &&
+                wait_bounded(wc, &bar_k_full[0], 0, 3);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        umma_commit(&bar_s_full[0]);
+        if (active1) {
+          issue_s(1, 0);
+          umma_commit(&bar_s_full[1]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::NST;
+        if (j + 1 < n_kv) {
+          const int st1 = (j + 1) % C::NST;
+          if (!wait_bounded(wc, &bar_k_full[st1], ((j + 1) / C::NST) & 1, 4)) break;
+          for (int s = 0; s < kSlots; ++s) {
+            if (j + 1 >= (s ? nkv1 : nkv0)) continue;
+            if (!wait_bounded(wc, &bar_s_free[s], j & 1, 5)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(s, st1);
+            umma_commit(&bar_s_full[s]);
+          }
+          if (!ok) break;
+        }
+        if (!wait_bounded(wc, &bar_v_full[st], (j / C::NST) & 1, 7)) break;
+        for (int s = 0; s < kSlots; ++s) {
+          if (j >= (s ? nkv1 : nkv0)) continue;
+          if (!wait_bounded(wc, &bar_p_full[s], j & 1, 6)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(s, st, j > 0);
+          umma_commit(&bar_o_done[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bar_kv_empty[st]);
+      }
+      // every issued MMA completes before TMEM is released (also on abort)
+      uint64_t* bar_fin = bar_o_done + kSlots;
+      umma_commit(bar_fin);
+      wait_drain(wc, bar_fin, 0, 13);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int slot = warp >> 2;
+    const int r = threadIdx.x & 127;  // query row within the tile == TMEM lane
+    const int qt = 2 * pair + slot;
+    const int nkv = slot ? nkv1 : nkv0;
+    const int qrow = qt * kBM + r;
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + slot * 256 + lane_off;
+    const uint32_t tO = tS + 128;
+    float m = -INFINITY;
+    float l = 0.f;
+    bool ok = nkv > 0;
+    uint8_t* prow = sP + slot * C::P_BYTES + r * 128;
+    const int sw = r & 7;
+    for (int j = 0; j < nkv; ++j) {
+      if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_s_full[slot], j & 1, 8))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]);
+        tmem_ld32(tS + c * 32, chunk);
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bar_s_free[slot]);
+
+      const bool diag = (j == nkv - 1);
+      const int kbase = j * kBN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        float v = __uint_as_float(sv[c]) * p.scale_log2;
+        if (diag && (kbase + c > qrow)) v = -INFINITY;
+        sv[c] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+      m = m_new;
+
+      if (j > 0) {
+        // PV of the previous tile must be finished before the P tile is
+        // overwritten and O is rescaled.
+        if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (j - 1) & 1, 9))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // P = exp2(s - m) rounded to T, streamed into the swizzled K-major tile:
+      // two 64-key halves of [128 rows][128 B]; 16-byte chunk ch of row r
+      // lives at chunk ch ^ (r & 7).
+      float sum = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c0 = half * 64 + ch * 8;
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            e[i] = fast_exp2(__uint_as_float(sv[c0 + i]) - m_new);
+            sum += e[i];
+          }
+          uint4 w;
+          w.x = pack2<T>(e[0], e[1]);
+          w.y = pack2<T>(e[2], e[3]);
+          w.z = pack2<T>(e[4], e[5]);
+          w.w = pack2<T>(e[6], e[7]);
+          *reinterpret_cast<uint4*>(prow + half * (kBM * 128) + ((ch ^ sw) * 16)) = w;
+        }
+      }
+      l = l * alpha + sum;
+      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t ov[16];
+          tmem_ld16(tO + c * 16, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st16(tO + c * 16, ov);
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_p_full[slot]);
+    }
+    // epilogue: O / l -> global, logsumexp (natural log of scaled scores)
+    if (ok && __all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (nkv - 1) & 1, 10))) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      T* orow = static_cast<T*>(p.o) + int64_t(b) * p.os[0] + int64_t(h) * p.os[1] + int64_t(qrow) * p.os[2];
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t ov[16];
+        tmem_ld16(tO + c * 16, ov);
+        tmem_ld_wait();
+        if (qrow < p.T) {
+          uint4 w0, w1;
+          w0.x = pack2<T>(__uint_as_float(ov[0]) * inv_l, __uint_as_float(ov[1]) * inv_l);
+          w0.y = pack2<T>(__uint_as_float(ov[2]) * inv_l, __uint_as_float(ov[3]) * inv_l);
+          w0.z = pack2<T>(__uint_as_float(ov[4]) * inv_l, __uint_as_float(ov[5]) * inv_l);
+          w0.w = pack2<T>(__uint_as_float(ov[6]) * inv_l, __uint_as_float(ov[7]) * inv_l);
+          w1.x = pack2<T>(__uint_as_float(ov[8]) * inv_l, __uint_as_float(ov[9]) * inv_l);
+          w1.y = pack2<T>(__uint_as_float(ov[10]) * inv_l, __uint_as_float(ov[11]) * inv_l);
+          w1.z = pack2<T>(__uint_as_float(ov[12]) * inv_l, __uint_as_float(ov[13]) * inv_l);
+          w1.w = pack2<T>(__uint_as_float(ov[14]) * inv_l, __uint_as_float(ov[15]) * inv_l);
+          *reinterpret_cast<uint4*>(orow + c * 16) = w0;
+          *reinterpret_cast<uint4*>(orow + c * 16 + 8) = w1;
+        }
+      }
+      if (qrow < p.T)
+        p.lse[(int64_t(b) * p.Hq + h) * p.T + qrow] = (m + __log2f(l)) * 0.69314718055994530942f;
+    }
+  }
+
+  // teardown: every role reaches this point (bounded waits never hang)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <typename T, int D>
+int launch_fwd(const FwdParams& prm, int B, int Hq, cudaStream_t stream) {
+  using C = FwdCfg<D>;
+  auto kern = attn_fwd_kernel<T, D>;
+  int st = set_smem_limit((const void*)kern, C::SMEM);
+  if (st != MT_OK) return st;
+  dim3 grid((unsigned)(B * Hq), (unsigned)prm.n_pairs);
+  kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
+  return check_launch("attention_fwd");
+}
+
+}  // namespace
+
+// Build a 4-D tensor map over a [B, H, T, D] tensor given element strides;
+// the two middle dimensions are ordered by stride.  Returns MT status.
+// swapped: -1 = choose from the strides (head stride below time stride, as in
+// the model's [B, T, H, D] layout), else force the given order.
+int make_bhtd_map(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t H, int64_t T, int64_t D,
+                  const int64_t* s, int box_rows, int* swapped) {
+  const int64_t es = 2;
+  const bool sw = (*swapped >= 0) ? (*swapped != 0) : (s[1] < s[2]);
+  uint64_t dims[4], strides[3];
+  uint32_t box[4];
+  dims[0] = D;
+  box[0] = (uint32_t)D;
+  if (sw) {
+    dims[1] = H; dims[2] = T; strides[0] = s[1] * es; strides[1] = s[2] * es;
+    box[1] = 1; box[2] = (uint32_t)box_rows;
+  } else {
+    dims[1] = T; dims[2] = H; strides[0] = s[2] * es; strides[1] = s[1] * es;
+    box[1] = (uint32_t)box_rows; box[2] = 1;
+  }
+  dims[3] = B;
+  strides[2] = s[0] * es;
+  box[3] = 1;
+  *swapped = sw ? 1 : 0;
+  const CUtensorMapDataType dt = dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapSwizzle swz = D == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return encode_tensor_map(map, dt, 4, const_cast<void*>(base), dims, strides, box, swz);
+}
+
+// Shared validation for the attention entry points.
+int check_attn_layout(const void* ptr, const int64_t* s, bool need) {
+  if (!need) return MT_OK;
+  if (ptr == nullptr || s == nullptr) return MT_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return MT_ERR_UNSUPPORTED_LAYOUT;
+  if (s[3] != 1) return MT_ERR_UNSUPPORTED_LAYOUT;
+  for (int i = 0; i < 3; ++i)
+    if (s[i] % 8 != 0 || s[i] <= 0) return MT_ERR_UNSUPPORTED_LAYOUT;
+  return MT_OK;
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int mt_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype,
+                                int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* qs,
+                                const int64_t* ks, const int64_t* vs, const int64_t* os, float scale,
+                                uint32_t* status, void* stream) {
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || (Hq % Hkv) != 0) return MT_ERR_INVALID_ARGUMENT;
+  if (D != 64 && D != 32) return MT_ERR_INVALID_ARGUMENT;
+  if (B == 0 || T == 0) return MT_OK;
+  if (lse == nullptr || status == nullptr) return MT_ERR_INVALID_ARGUMENT;
+  if (B * Hq > 0x7fffffff || T > (int64_t(1) << 30)) return MT_ERR_INVALID_ARGUMENT;
+  int st = MT_OK;
+  if ((st = check_attn_layout(q, qs, true)) != MT_OK) return st;
+  if ((st = check_attn_layout(k, ks, true)) != MT_OK) return st;
+  if ((st = check_attn_layout(v, vs, true)) != MT_OK) return st;
+  if ((st = check_attn_layout(o, os, true)) != MT_OK) return st;
+  if ((st = check_arch()) != MT_OK) return st;
+  FwdParams prm;
+  // One coordinate order per launch: chosen from q's strides, applied to k/v
+  // (a size-1 head or time dimension makes either order valid).
+  int swq = (Hq == 1 || T == 1) ? ((Hkv > 1 && T > 1) ? (ks[1] < ks[2] ? 1 : 0) : 0) : -1;
+  if ((st = make_bhtd_map(&prm.tm_q, q, dtype, B, Hq, T, D, qs, kBM, &swq)) != MT_OK) return st;
+  int swk = swq, swv = swq;
+  if (Hkv > 1 && T > 1 && ((ks[1] < ks[2]) != (swq != 0) || (vs[1] < vs[2]) != (swq != 0)))
+    return MT_ERR_UNSUPPORTED_LAYOUT;
+  if ((st = make_bhtd_map(&prm.tm_k, k, dtype, B, Hkv, T, D, ks, kBN, &swk)) != MT_OK) return st;
+  if ((st = make_bhtd_map(&prm.tm_v, v, dtype, B, Hkv, T, D, vs, kBN, &swv)) != MT_OK) return st;
+  prm.ht_swapped = swq;
+  prm.o = o;
+  prm.lse = lse;
+  for (int i = 0; i < 4; ++i) prm.os[i] = os[i];
+  prm.T = (int)T;
+  prm.Hq = (int)Hq;
+  prm.Hkv = (int)Hkv;
+  prm.repeats = (int)(Hq / Hkv);
+  prm.n_qtiles = (int)((T + kBM - 1) / kBM);
+  prm.n_pairs = (prm.n_qtiles + 1) / 2;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.status = status;
+  if (prm.n_qtiles > 65535) return MT_ERR_INVALID_ARGUMENT;
+  auto s = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == MT_BF16;
+  if (D == 64) return bf ? launch_fwd<__nv_bfloat16, 64>(prm, (int)B, (int)Hq, s) : launch_fwd<__half, 64>(prm, (int)B, (int)Hq, s);
+  return bf ? launch_fwd<__nv_bfloat16, 32>(prm, (int)B, (int)Hq, s) : launch_fwd<__half, 32>(prm, (int)B, (int)Hq, s);
+}

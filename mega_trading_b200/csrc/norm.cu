@@ -1,0 +1,473 @@
+// RMSNorm and fused residual-add + RMSNorm, forward and backward.
+//
+// Reference semantics (duoan/mega-trading):
+//   forward  src/mega_trading/kernels/triton_ops.py:528-538 (RMSNorm),
+//            :541-566 (add+RMSNorm); torch path F.rms_norm (model.py:269)
+//   backward :633-665 and :569-608, dW finished by a torch sum (:183, :287)
+//
+// B200 design: one warp per row, 16-byte vector loads (8 elements per lane
+// per chunk), the row held in registers between the reduction and the
+// normalisation, warp-shuffle reductions, fp32 math for every dtype.  The
+// backward keeps per-lane dW partials in registers across the rows a warp
+// visits, reduces the 8 warps of a block through shared memory and writes one
+// fp32 partial row per block into the caller's workspace; a second small
+// kernel sums the partials in a fixed order (deterministic dW).
+#include "common.cuh"
+
+namespace mt {
+namespace {
+
+constexpr int kWarps = 8;           // rows in flight per block
+constexpr int kChunk = 8;           // elements per lane per chunk
+constexpr int kBwdBlocksPerSM = 2;  // persistent backward grid
+
+// Load / store 8 consecutive elements as floats (16 or 32 bytes).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    load_vec<T, 8>(p, v);
+  } else {
+    float a[4], b[4];
+    load_vec<T, 4>(p, a);
+    load_vec<T, 4>(p + 4, b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = a[i];
+      v[i + 4] = b[i];
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    store_vec<T, 8>(p, v);
+  } else {
+    float a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = v[i];
+      b[i] = v[i + 4];
+    }
+    store_vec<T, 4>(p, a);
+    store_vec<T, 4>(p + 4, b);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward: vectorised, row in registers (NC chunks of 8 per lane)
+//   ADD: s = round_to<TR>(x + r) is stored as new_residual and normalised.
+// ---------------------------------------------------------------------------
+template <typename TX, typename TW, typename TY, typename TR, bool ADD, int NC>
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_vec(const TX* __restrict__ x, const TX* __restrict__ r,
+                                                           const TW* __restrict__ w, TR* __restrict__ new_res,
+                                                           TY* __restrict__ y, float* __restrict__ rstd,
+                                                           int64_t rows, int dim, float eps) {
+  const int lane = lane_id();
+  const int64_t row = int64_t(blockIdx.x) * kWarps + warp_id();
+  if (row >= rows) return;
+  const TX* xr = x + row * dim;
+  float v[NC][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * kChunk;
+    if (col < dim) {
+      load8<TX>(xr + col, v[c]);
+      if constexpr (ADD) {
+        float rv[8];
+        load8<TX>(r + row * dim + col, rv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = round_to<TR>(v[c][i] + rv[i]);
+        store8<TR>(new_res + row * dim + col, v[c]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / float(dim) + eps);
+  if (lane == 0) rstd[row] = inv;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * kChunk;
+    if (col < dim) {
+      float wv[8], o[8];
+      load8<TW>(w + col, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * inv * wv[i];
+      store8<TY>(y + row * dim + col, o);
+    }
+  }
+}
+
+// Generic forward (any dim / alignment): one warp per row, scalar accesses,
+// two passes over the row.
+template <typename TX, typename TW, typename TY, typename TR, bool ADD>
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restrict__ x, const TX* __restrict__ r,
+                                                              const TW* __restrict__ w, TR* __restrict__ new_res,
+                                                              TY* __restrict__ y, float* __restrict__ rstd,
+                                                              int64_t rows, int dim, float eps) {
+  const int lane = lane_id();
+  const int64_t row = int64_t(blockIdx.x) * kWarps + warp_id();
+  if (row >= rows) return;
+  float ss = 0.f;
+  for (int col = lane; col < dim; col += 32) {
+    float s = to_f32<TX>(x[row * dim + col]);
+    if constexpr (ADD) {
+      s = round_to<TR>(s + to_f32<TX>(r[row * dim + col]));
+      new_res[row * dim + col] = from_f32<TR>(s);
+    }
+    ss = fmaf(s, s, ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / float(dim) + eps);
+  if (lane == 0) rstd[row] = inv;
+  for (int col = lane; col < dim; col += 32) {
+    float s = to_f32<TX>(x[row * dim + col]);
+    if constexpr (ADD) s = round_to<TR>(s + to_f32<TX>(r[row * dim + col]));
+    y[row * dim + col] = from_f32<TY>(s * inv * to_f32<TW>(w[col]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward: persistent grid, warps stride over rows.
+//   dn   = dy * w
+//   dx   = rstd * (dn - x * rstd^2 * sum(dn * x) / dim)  (+ g_res if GRES)
+//   dw_p = sum_rows dy * x * rstd                       (per block partial)
+// ---------------------------------------------------------------------------
+template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES, int NC>
+__global__ void __launch_bounds__(kWarps * 32) rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w,
+                                                           const float* __restrict__ rstd, const TG* __restrict__ dy,
+                                                           const TGR* __restrict__ gres, TD* __restrict__ dx,
+                                                           float* __restrict__ partial, int64_t rows, int dim) {
+  extern __shared__ float red[];  // [kWarps][dim]
+  const int lane = lane_id();
+  const int warp = warp_id();
+  float wv[NC][8];
+  float acc[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * kChunk;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
+    if (col < dim) load8<TW>(w + col, wv[c]);
+  }
+  for (int64_t row = int64_t(blockIdx.x) * kWarps + warp; row < rows; row += int64_t(gridDim.x) * kWarps) {
+    const float inv = rstd[row];
+    float xv[NC][8], gv[NC][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * kChunk;
+      if (col < dim) {
+        load8<TX>(x + row * dim + col, xv[c]);
+        load8<TG>(dy + row * dim + col, gv[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          dot = fmaf(gv[c][i] * wv[c][i], xv[c][i], dot);
+          acc[c][i] = fmaf(gv[c][i], xv[c][i] * inv, acc[c][i]);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float k = inv * inv * dot / float(dim);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * kChunk;
+      if (col < dim) {
+        float o[8];
+        float gr[8];
+        if constexpr (GRES) load8<TGR>(gres + row * dim + col, gr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[i] = inv * (gv[c][i] * wv[c][i] - xv[c][i] * k);
+          if constexpr (GRES) o[i] += gr[i];
+        }
+        store8<TD>(dx + row * dim + col, o);
+      }
+    }
+  }
+  // block reduction of the dW partials
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * kChunk;
+    if (col < dim) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red[warp * dim + col + i] = acc[c][i];
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kWarps; ++q) s += red[q * dim + col];
+    partial[int64_t(blockIdx.x) * dim + col] = s;
+  }
+}
+
+template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES>
+__global__ void __launch_bounds__(kWarps * 32) rms_bwd_scalar(const TX* __restrict__ x, const TW* __restrict__ w,
+                                                              const float* __restrict__ rstd,
+                                                              const TG* __restrict__ dy, const TGR* __restrict__ gres,
+                                                              TD* __restrict__ dx, float* __restrict__ partial,
+                                                              int64_t rows, int dim) {
+  // dW partial per block: thread t owns columns t, t + blockDim, ... and
+  // loops over the block's rows itself (no cross-warp reduction needed).
+  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+    float s = 0.f;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x)
+      s += to_f32<TG>(dy[row * dim + col]) * to_f32<TX>(x[row * dim + col]) * rstd[row];
+    partial[int64_t(blockIdx.x) * dim + col] = s;
+  }
+  const int lane = lane_id();
+  for (int64_t row = int64_t(blockIdx.x) * kWarps + warp_id(); row < rows; row += int64_t(gridDim.x) * kWarps) {
+    const float inv = rstd[row];
+    float dot = 0.f;
+    for (int col = lane; col < dim; col += 32)
+      dot += to_f32<TG>(dy[row * dim + col]) * to_f32<TW>(w[col]) * to_f32<TX>(x[row * dim + col]);
+    dot = warp_sum(dot);
+    const float k = inv * inv * dot / float(dim);
+    for (int col = lane; col < dim; col += 32) {
+      float o = inv * (to_f32<TG>(dy[row * dim + col]) * to_f32<TW>(w[col]) - to_f32<TX>(x[row * dim + col]) * k);
+      if constexpr (GRES) o += to_f32<TGR>(gres[row * dim + col]);
+      dx[row * dim + col] = from_f32<TD>(o);
+    }
+  }
+}
+
+template <typename TW>
+__global__ void dw_reduce(const float* __restrict__ partial, int nblocks, int dim, TW* __restrict__ dw) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= dim) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += partial[int64_t(b) * dim + col];
+  dw[col] = from_f32<TW>(s);
+}
+
+// ---------------------------------------------------------------------------
+// dispatch helpers
+// ---------------------------------------------------------------------------
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename F>
+int with_dtype(int code, F&& f) {
+  switch (code) {
+    case MT_F32: return f(float{});
+    case MT_F16: return f(__half{});
+    case MT_BF16: return f(__nv_bfloat16{});
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int chunks_for(int64_t dim) {
+  const int64_t per_lane = (dim + 32 * kChunk - 1) / (32 * kChunk);
+  if (per_lane <= 1) return 1;
+  if (per_lane <= 2) return 2;
+  if (per_lane <= 4) return 4;
+  if (per_lane <= 8) return 8;
+  return 0;  // too wide for the register-resident path
+}
+
+template <bool ADD, typename TX, typename TW, typename TY, typename TR>
+int launch_fwd(const void* x, const void* r, const void* w, void* new_res, void* y, float* rstd, int64_t rows,
+               int64_t dim, float eps, cudaStream_t stream) {
+  const int nc = chunks_for(dim);
+  const bool vec = nc > 0 && dim % kChunk == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
+                   (!ADD || (aligned16(r) && aligned16(new_res)));
+  const dim3 grid((unsigned)((rows + kWarps - 1) / kWarps));
+  const dim3 block(kWarps * 32);
+  auto X = static_cast<const TX*>(x);
+  auto R = static_cast<const TX*>(r);
+  auto W = static_cast<const TW*>(w);
+  auto NR = static_cast<TR*>(new_res);
+  auto Y = static_cast<TY*>(y);
+  const int d = (int)dim;
+  if (vec) {
+    switch (nc) {
+      case 1: rms_fwd_vec<TX, TW, TY, TR, ADD, 1><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+      case 2: rms_fwd_vec<TX, TW, TY, TR, ADD, 2><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+      case 4: rms_fwd_vec<TX, TW, TY, TR, ADD, 4><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+      default: rms_fwd_vec<TX, TW, TY, TR, ADD, 8><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+    }
+  } else {
+    rms_fwd_scalar<TX, TW, TY, TR, ADD><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps);
+  }
+  return check_launch(ADD ? "add_rms_norm_fwd" : "rms_norm_fwd");
+}
+
+int bwd_blocks(int64_t rows) {
+  int64_t g = int64_t(get_sm_count()) * kBwdBlocksPerSM;
+  const int64_t need = (rows + kWarps - 1) / kWarps;
+  if (g > need) g = need;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <bool GRES, typename TX, typename TW, typename TG, typename TGR, typename TD, typename TDW>
+int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* gres, void* dx, void* dw,
+               void* workspace, int64_t ws_bytes, int64_t rows, int64_t dim, cudaStream_t stream) {
+  const int nblocks = bwd_blocks(rows);
+  if (workspace == nullptr || ws_bytes < int64_t(nblocks) * dim * 4) return MT_ERR_WORKSPACE;
+  float* partial = static_cast<float*>(workspace);
+  const int nc = chunks_for(dim);
+  const bool vec = nc > 0 && dim % kChunk == 0 && aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dx) &&
+                   (!GRES || aligned16(gres));
+  auto X = static_cast<const TX*>(x);
+  auto W = static_cast<const TW*>(w);
+  auto G = static_cast<const TG*>(dy);
+  auto GR = static_cast<const TGR*>(gres);
+  auto DX = static_cast<TD*>(dx);
+  const int d = (int)dim;
+  const int smem = kWarps * d * 4;
+  if (vec) {
+    const void* fn = nullptr;
+    switch (nc) {
+      case 1: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1>; break;
+      case 2: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2>; break;
+      case 4: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4>; break;
+      default: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8>; break;
+    }
+    int st = set_smem_limit(fn, smem);
+    if (st != MT_OK) return st;
+    switch (nc) {
+      case 1: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      case 2: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      case 4: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      default: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+    }
+  } else {
+    rms_bwd_scalar<TX, TW, TG, TGR, TD, GRES><<<nblocks, kWarps * 32, 0, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d);
+  }
+  int st = check_launch(GRES ? "add_rms_norm_bwd" : "rms_norm_bwd");
+  if (st != MT_OK) return st;
+  dw_reduce<TDW><<<(d + 255) / 256, 256, 0, stream>>>(partial, nblocks, d, static_cast<TDW*>(dw));
+  return check_launch("rms_norm_dw_reduce");
+}
+
+int validate_rows(const void* a, const void* b, int64_t rows, int64_t dim) {
+  if (rows < 0 || dim <= 0 || dim > (1 << 20)) return MT_ERR_INVALID_ARGUMENT;
+  if (rows > 0 && (a == nullptr || b == nullptr)) return MT_ERR_INVALID_ARGUMENT;
+  return MT_OK;
+}
+
+// Supported dtype combinations (x, w, y[, residual]): the all-same-dtype
+// cases of the reference API plus the mixed cases of the B200 training step
+// (fp32 residual stream, fp32 weights, bf16 normalised output).
+#define MT_DT(a) ((a) & 3)
+constexpr int key3(int a, int b, int c) { return (a << 4) | (b << 2) | c; }
+constexpr int key5(int a, int b, int c, int d, int e) { return (a << 8) | (b << 6) | (c << 4) | (d << 2) | e; }
+
+}  // namespace
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" {
+
+int mt_rms_norm_fwd(const void* x, int x_dtype, const void* w, int w_dtype, void* y, int y_dtype, float* rstd,
+                    int64_t rows, int64_t dim, float eps, void* stream) {
+  int st = validate_rows(x, y, rows, dim);
+  if (st != MT_OK) return st;
+  if (rows == 0) return MT_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  using bf = __nv_bfloat16;
+  using hf = __half;
+  switch (key3(x_dtype, w_dtype, y_dtype)) {
+#define CASE(a, b, c, TA, TB, TC) \
+  case key3(a, b, c): return launch_fwd<false, TA, TB, TC, TA>(x, nullptr, w, nullptr, y, rstd, rows, dim, eps, s);
+    CASE(MT_BF16, MT_BF16, MT_BF16, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, bf, float, bf)
+    CASE(MT_F16, MT_F32, MT_F16, hf, float, hf)
+    CASE(MT_F32, MT_F32, MT_BF16, float, float, bf)
+#undef CASE
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int64_t mt_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t dim) {
+  return int64_t(bwd_blocks(rows)) * dim * 4;
+}
+
+static int zero_dw(void* dw, int dw_dtype, int64_t dim, cudaStream_t s) {
+  const int64_t esize = dw_dtype == MT_F32 ? 4 : 2;
+  cudaError_t e = cudaMemsetAsync(dw, 0, dim * esize, s);
+  return e == cudaSuccess ? MT_OK : MT_ERR_LAUNCH;
+}
+
+int mt_rms_norm_bwd(const void* x, int x_dtype, const void* w, int w_dtype, const float* rstd, const void* dy,
+                    int dy_dtype, void* dx, int dx_dtype, void* dw, int dw_dtype, void* workspace,
+                    int64_t workspace_bytes, int64_t rows, int64_t dim, void* stream) {
+  int st = validate_rows(x, dx, rows, dim);
+  if (st != MT_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) return zero_dw(dw, dw_dtype, dim, s);
+  using bf = __nv_bfloat16;
+  using hf = __half;
+  switch (key5(x_dtype, w_dtype, dy_dtype, dx_dtype, dw_dtype)) {
+#define CASE(a, b, c, d, e, TA, TB, TC, TD, TE)                                                               \
+  case key5(a, b, c, d, e):                                                                                    \
+    return launch_bwd<false, TA, TB, TC, TC, TD, TE>(x, w, rstd, dy, nullptr, dx, dw, workspace, workspace_bytes, \
+                                                 rows, dim, s);
+    CASE(MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, bf, bf, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, hf, hf, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, float, float, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, MT_BF16, MT_F32, bf, float, bf, bf, float)
+    CASE(MT_F16, MT_F32, MT_F16, MT_F16, MT_F32, hf, float, hf, hf, float)
+    CASE(MT_F32, MT_F32, MT_BF16, MT_F32, MT_F32, float, float, bf, float, float)
+#undef CASE
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int mt_add_rms_norm_fwd(const void* hidden, const void* residual, int act_dtype, const void* w, int w_dtype,
+                        void* new_residual, int res_dtype, void* normed, int normed_dtype, float* rstd, int64_t rows,
+                        int64_t dim, float eps, void* stream) {
+  int st = validate_rows(hidden, normed, rows, dim);
+  if (st != MT_OK) return st;
+  if (rows > 0 && (residual == nullptr || new_residual == nullptr)) return MT_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return MT_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  using bf = __nv_bfloat16;
+  using hf = __half;
+  if (res_dtype != act_dtype) return MT_ERR_UNSUPPORTED_DTYPE;
+  switch (key3(act_dtype, w_dtype, normed_dtype)) {
+#define CASE(a, b, c, TA, TB, TC)                                                                                  \
+  case key3(a, b, c):                                                                                              \
+    return launch_fwd<true, TA, TB, TC, TA>(hidden, residual, w, new_residual, normed, rstd, rows, dim, eps, s);
+    CASE(MT_BF16, MT_BF16, MT_BF16, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, bf, float, bf)
+    CASE(MT_F32, MT_F32, MT_BF16, float, float, bf)
+#undef CASE
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, int w_dtype, const float* rstd,
+                        const void* grad_new_residual, int gres_dtype, const void* grad_normed, int gnorm_dtype,
+                        void* grad_input, int gin_dtype, void* dw, int dw_dtype, void* workspace,
+                        int64_t workspace_bytes, int64_t rows, int64_t dim, void* stream) {
+  int st = validate_rows(new_residual, grad_input, rows, dim);
+  if (st != MT_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) return zero_dw(dw, dw_dtype, dim, s);
+  using bf = __nv_bfloat16;
+  using hf = __half;
+  switch (key5(res_dtype, w_dtype, gnorm_dtype, gres_dtype, gin_dtype) | (dw_dtype << 10)) {
+#define CASE(a, b, c, d, e, f, TA, TB, TC, TD, TE, TF)                                                          \
+  case key5(a, b, c, d, e) | (f << 10):                                                                          \
+    return launch_bwd<true, TA, TB, TC, TE, TF, TD>(new_residual, w, rstd, grad_normed, grad_new_residual,       \
+                                                    grad_input, dw, workspace, workspace_bytes, rows, dim, s);
+    CASE(MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, bf, bf, bf, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, hf, hf, hf, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, float, float, float, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, MT_BF16, MT_BF16, MT_F32, bf, float, bf, bf, bf, float)
+    CASE(MT_F32, MT_F32, MT_BF16, MT_F32, MT_F32, MT_F32, float, float, bf, float, float, float)
+#undef CASE
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+"""B200 (sm_100a) causal grouped-query attention.
+
+Drop-in mirror of ``mega_trading.kernels.triton_attention`` (duoan/mega-trading,
+``src/mega_trading/kernels/triton_attention.py:12-111``): same function name,
+signature, validation messages and autograd contract.  Forward and backward
+are tcgen05/TMEM/TMA kernels for every shape with head_dim 32 or 64 in bf16 or
+fp16 (the reference's Triton backward only covers one shape and otherwise
+materialises fp32 T x T tensors, ``triton_attention.py:85-111``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _lib
+
+__all__ = ["triton_attention", "attention"]
+
+_SUPPORTED = {torch.bfloat16, torch.float16}
+
+
+def _launch_fwd(q, k, v, repeats: int, scale: float):
+    lib = _lib.load()
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, T), device=q.device, dtype=torch.float32)
+    status = _lib.status_word(q.device)
+    st = lib.mt_attention_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), _lib.dtype_code(q.dtype),
+        B, Hq, Hkv, T, D, _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
+        _lib.i64_array(o.stride()), float(scale), status.data_ptr(), _lib.stream_ptr(q.device),
+    )
+    _lib.check(st, "attention forward")
+    _lib.count(1)
+    return o, lse
+
+
+def _launch_bwd(q, k, v, o, lse, do, scale: float):
+    lib = _lib.load()
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    ws_bytes = int(lib.mt_attention_bwd_workspace_bytes(B, Hq, T, D))
+    ws = torch.empty((max(ws_bytes, 16),), device=q.device, dtype=torch.uint8)
+    status = _lib.status_word(q.device)
+    st = lib.mt_attention_bwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(), dq.data_ptr(),
+        dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), B, Hq, Hkv, T, D,
+        _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
+        _lib.i64_array(o.stride()), _lib.i64_array(do.stride()), _lib.i64_array(dq.stride()),
+        _lib.i64_array(dk.stride()), _lib.i64_array(dv.stride()), float(scale), ws.data_ptr(), ws.numel(),
+        status.data_ptr(), _lib.stream_ptr(q.device),
+    )
+    _lib.check(st, "attention backward")
+    _lib.count(3)
+    return dq, dk, dv
+
+
+def _aligned_view(t: torch.Tensor) -> torch.Tensor:
+    """Return ``t`` if the kernels accept its layout, else a contiguous copy."""
+    s = t.stride()
+    ok = s[3] == 1 and all(x % 8 == 0 and x > 0 for x in s[:3]) and t.data_ptr() % 16 == 0
+    return t if ok else t.contiguous()
+
+
+class _CausalAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, query, key, value, repeats):
+        q = _aligned_view(query)
+        k = _aligned_view(key)
+        v = _aligned_view(value)
+        scale = 1.0 / math.sqrt(q.shape[-1])
+        o, lse = _launch_fwd(q, k, v, repeats, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = _aligned_view(grad_output)
+        dq, dk, dv = _launch_bwd(q, k, v, o, lse, do, ctx.scale)
+        return dq, dk, dv, None
+
+
+def triton_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, *, repeats: int) -> torch.Tensor:
+    """Causal grouped-query attention on sm_100a (query [B,Hq,T,D], key/value [B,Hkv,T,D])."""
+    if query.device.type != "cuda":
+        raise RuntimeError("triton attention backend requires CUDA tensors")
+    if query.dtype not in {torch.float16, torch.bfloat16, torch.float32}:
+        raise RuntimeError("triton attention supports float16, bfloat16, and float32 tensors")
+    if key.shape[1] * repeats != query.shape[1]:
+        raise ValueError("query heads must equal key/value heads multiplied by repeats")
+    if key.shape != value.shape:
+        raise ValueError("key and value must have the same shape")
+    if query.shape[0] != key.shape[0] or query.shape[2:] != key.shape[2:]:
+        raise ValueError("query, key, and value must agree on batch, sequence, and head dimensions")
+    _lib.require_cuda_sm100(query, "triton_attention")
+    if query.dtype not in _SUPPORTED:
+        raise RuntimeError("the sm_100a attention kernels take float16 or bfloat16 tensors")
+    if key.dtype != query.dtype or value.dtype != query.dtype:
+        raise RuntimeError("query, key and value must share one dtype")
+    if query.shape[-1] not in (32, 64):
+        raise RuntimeError("the sm_100a attention kernels support head_dim 32 or 64")
+    return _CausalAttention.apply(query, key, value, int(repeats))
+
+
+attention = triton_attention
