@@ -570,6 +570,7 @@ extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, con
   if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MT_ERR_WORKSPACE;
   Workspace ws = carve(workspace, B, Hq, T, D);
   if (workspace_bytes < ws.bytes) return MT_ERR_WORKSPACE;
+  if ((st = bind_device_of(q)) != MT_OK) return st;
   if ((st = check_arch()) != MT_OK) return st;
 
   BwdParams prm;

@@ -445,6 +445,7 @@ extern "C" int mt_attention_fwd(const void* q, const void* k, const void* v, voi
   if ((st = check_attn_layout(k, ks, true)) != MT_OK) return st;
   if ((st = check_attn_layout(v, vs, true)) != MT_OK) return st;
   if ((st = check_attn_layout(o, os, true)) != MT_OK) return st;
+  if ((st = bind_device_of(q)) != MT_OK) return st;
   if ((st = check_arch()) != MT_OK) return st;
   FwdParams prm;
   // One coordinate order per launch: chosen from q's strides, applied to k/v

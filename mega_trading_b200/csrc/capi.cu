@@ -66,6 +66,39 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 EncodeTiledFn g_encode = nullptr;
 }  // namespace
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+
+int bind_device_of(const void* ptr) {
+  // A thread that has not touched CUDA yet (e.g. PyTorch's autograd worker
+  // for device 0) may have no current context; the driver-API tensor-map
+  // encoder needs one.  Bind the primary context of the device owning `ptr`.
+  if (g_ctx_get_current == nullptr) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_ctx_get_current == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess || fn == nullptr)
+        return MT_ERR_LAUNCH;
+      g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    }
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr) return MT_OK;
+  cudaPointerAttributes attr;
+  cudaError_t err = cudaPointerGetAttributes(&attr, ptr);
+  if (err != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+    set_last_error("cudaPointerGetAttributes", err);
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  err = cudaSetDevice(attr.device);
+  if (err != cudaSuccess) {
+    set_last_error("cudaSetDevice", err);
+    return MT_ERR_LAUNCH;
+  }
+  return MT_OK;
+}
+
 int check_arch() {
   int dev;
   int st = device_info(&dev);

@@ -18,6 +18,9 @@ namespace mt {
 void set_last_error(const char* where, cudaError_t err);
 int check_launch(const char* where);
 int check_arch();  // MT_OK on sm_100, MT_ERR_UNSUPPORTED_ARCH otherwise
+// Make the primary context of the device that owns `ptr` current on this
+// thread if no context is current (driver-API calls need one).
+int bind_device_of(const void* ptr);
 int get_sm_count();
 // Raise the dynamic shared memory limit of a kernel (once per device and
 // kernel) when a launch needs more than the default 48 KB.
