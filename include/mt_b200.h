@@ -170,6 +170,37 @@ MT_API int mt_attention_bwd(const void* q, const void* k, const void* v,
                      void* workspace, int64_t workspace_bytes, uint32_t* status,
                      void* stream);
 
+
+/* ---------------------------------------------------------------------
+ * Fused linear + cross-entropy   replaces triton_fused_linear_cross_entropy
+ *   (src/mega_trading/kernels/triton_ops.py:64-92, :294-411, row kernel
+ *    :822-887; torch path :99-112)
+ * hidden: [N, K] and weight: [V, K], contiguous, bf16 or fp16, K % 8 == 0;
+ * labels: [N] int64 (labels_i64 = 1) or int32; rows whose label equals
+ * ignore_index contribute no loss and no gradient.
+ *
+ * Forward: loss = mean over valid rows of (logsumexp(hidden W^T) - z_label),
+ * 0 when no row is valid.  The logits live only in TMEM/registers.
+ * lse2_out (optional): [N + 3] fp32 = per-row logsumexp in log2 units followed
+ * by {loss, n_valid, 1/n_valid}; it is the input of the backward.
+ * ------------------------------------------------------------------- */
+MT_API int64_t mt_fused_ce_workspace_bytes(int64_t N, int64_t V);
+MT_API int mt_fused_ce_fwd(const void* hidden, const void* weight, const void* labels,
+                           int labels_i64, int64_t ignore_index, int dtype, int64_t N,
+                           int64_t V, int64_t K, float* loss, float* lse2_out,
+                           void* workspace, int64_t workspace_bytes, uint32_t* status,
+                           void* stream);
+
+/* Backward part 1: dZ = (softmax(hidden W^T) - onehot(label)) / n_valid * grad_out
+ * written to dz ([N, dz_ld] row-major, dz_ld >= V, dz_ld % 8 == 0) in the input
+ * dtype; the logits are recomputed on chip.  grad_out: device fp32 scalar.
+ * The caller finishes with dH = dZ W and dW = dZ^T hidden. */
+MT_API int mt_fused_ce_grad_logits(const void* hidden, const void* weight,
+                                   const void* labels, int labels_i64,
+                                   int64_t ignore_index, int dtype, int64_t N, int64_t V,
+                                   int64_t K, const float* lse2_scal, const float* grad_out,
+                                   void* dz, int64_t dz_ld, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
