@@ -170,3 +170,41 @@ launches = 0
 def count(n: int) -> None:
     global launches
     launches += n
+
+
+class KernelTimer:
+    """Optional CUDA-event timing of named C-ABI calls on their launch stream."""
+
+    def __init__(self) -> None:
+        self.enabled = False
+        self.events: dict[str, list[tuple[torch.cuda.Event, torch.cuda.Event]]] = {}
+
+    def reset(self) -> None:
+        self.events = {}
+
+    def start(self, name: str, device: torch.device):
+        if not self.enabled:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(device))
+        return (name, ev, device)
+
+    def stop(self, token) -> None:
+        if token is None:
+            return
+        name, ev, device = token
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(torch.cuda.current_stream(device))
+        self.events.setdefault(name, []).append((ev, end))
+
+    def summary(self) -> dict[str, tuple[int, float]]:
+        """name -> (launches, mean milliseconds); synchronises the device."""
+        torch.cuda.synchronize()
+        out = {}
+        for name, pairs in self.events.items():
+            total = sum(a.elapsed_time(b) for a, b in pairs)
+            out[name] = (len(pairs), total / max(len(pairs), 1))
+        return out
+
+
+timer = KernelTimer()

@@ -31,11 +31,13 @@ class _FusedLinearCrossEntropy(torch.autograd.Function):
         loss = torch.empty((), device=dev, dtype=torch.float32)
         lse2 = torch.empty((n + 3,), device=dev, dtype=torch.float32)
         ws = torch.empty((int(lib.mt_fused_ce_workspace_bytes(n, v)),), device=dev, dtype=torch.uint8)
+        tok = _lib.timer.start("fused_ce_fwd", dev)
         st = lib.mt_fused_ce_fwd(
             h.data_ptr(), w.data_ptr(), lab.data_ptr(), 1 if lab.dtype == torch.int64 else 0, int(ignore_index),
             _lib.dtype_code(cdtype), n, v, k, loss.data_ptr(), lse2.data_ptr(), ws.data_ptr(), ws.numel(),
             _lib.status_word(dev).data_ptr(), _lib.stream_ptr(dev),
         )
+        _lib.timer.stop(tok)
         _lib.check(st, "fused linear cross-entropy forward")
         _lib.count(3)
         ctx.save_for_backward(h, w, lab, lse2)
@@ -57,11 +59,13 @@ class _FusedLinearCrossEntropy(torch.autograd.Function):
         ld = (v + 7) // 8 * 8
         dz = torch.empty((n, ld), device=dev, dtype=h.dtype)
         go = grad_output.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+        tok = _lib.timer.start("fused_ce_grad_logits", dev)
         st = lib.mt_fused_ce_grad_logits(
             h.data_ptr(), w.data_ptr(), lab.data_ptr(), 1 if lab.dtype == torch.int64 else 0, ctx.ignore_index,
             _lib.dtype_code(h.dtype), n, v, k, lse2.data_ptr(), go.data_ptr(), dz.data_ptr(), ld,
             _lib.status_word(dev).data_ptr(), _lib.stream_ptr(dev),
         )
+        _lib.timer.stop(tok)
         _lib.check(st, "fused linear cross-entropy backward")
         _lib.count(1)
         dzv = dz[:, :v]

@@ -28,11 +28,13 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     o = torch.empty_like(q)
     lse = torch.empty((B, Hq, T), device=q.device, dtype=torch.float32)
     status = _lib.status_word(q.device)
+    tok = _lib.timer.start("attention_fwd", q.device)
     st = lib.mt_attention_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), _lib.dtype_code(q.dtype),
         B, Hq, Hkv, T, D, _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
         _lib.i64_array(o.stride()), float(scale), status.data_ptr(), _lib.stream_ptr(q.device),
     )
+    _lib.timer.stop(tok)
     _lib.check(st, "attention forward")
     _lib.count(1)
     return o, lse
@@ -48,6 +50,7 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float):
     ws_bytes = int(lib.mt_attention_bwd_workspace_bytes(B, Hq, T, D))
     ws = torch.empty((max(ws_bytes, 16),), device=q.device, dtype=torch.uint8)
     status = _lib.status_word(q.device)
+    tok = _lib.timer.start("attention_bwd", q.device)
     st = lib.mt_attention_bwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(), dq.data_ptr(),
         dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), B, Hq, Hkv, T, D,
@@ -56,6 +59,7 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float):
         _lib.i64_array(dk.stride()), _lib.i64_array(dv.stride()), float(scale), ws.data_ptr(), ws.numel(),
         status.data_ptr(), _lib.stream_ptr(q.device),
     )
+    _lib.timer.stop(tok)
     _lib.check(st, "attention backward")
     _lib.count(3)
     return dq, dk, dv

@@ -1,0 +1,88 @@
+"""Data-parallel training step for the B200 model.
+
+Mirrors the reference's hot loop (``src/mega_trading/trainer.py:324-345``):
+forward, next-token cross-entropy (here the fused kernel, closing the wiring
+gap at ``trainer.py:337-338``), backward with the bucketed NCCL gradient
+all-reduce overlapped with backward (torch DDP, as Accelerate's default
+``trainer.py:1009-1023, :300-308``), fused AdamW (``trainer.py:537-545``).
+One process per GPU; the batch is split across ranks and, inside a rank,
+across micro-batches (gradient accumulation, all-reduce on the last one).
+The all-reduce is the only collective of the step.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+from .model import ModelConfig, TradingModelB200
+
+
+def init_distributed(backend: str = "nccl", timeout_s: int = 300) -> tuple[int, int, int]:
+    """Initialise the default process group from torchrun's environment; returns
+    ``(rank, world_size, local_rank)`` (``(0, 1, 0)`` without torchrun)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1:
+        return 0, 1, 0
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+        if backend == "nccl":
+            kwargs["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend=backend, **kwargs)
+    return rank, world, local
+
+
+class Trainer:
+    """Owns the model replica, the DDP wrapper and the optimizer of one rank."""
+
+    def __init__(self, cfg: ModelConfig, *, micro_batch: int, device: torch.device, lr: float = 2e-4,
+                 weight_decay: float = 0.01, seed: int = 0, bucket_cap_mb: int = 64,
+                 model: torch.nn.Module | None = None) -> None:
+        torch.manual_seed(seed)  # identical initial replicas on every rank
+        self.cfg = cfg
+        self.device = device
+        self.micro_batch = int(micro_batch)
+        # `model` lets host-side tests drive the same DP logic with another module
+        self.model = (model if model is not None else TradingModelB200(cfg)).to(device)
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        if self.world > 1:
+            self.engine = torch.nn.parallel.DistributedDataParallel(
+                self.model,
+                device_ids=[device.index] if device.type == "cuda" else None,
+                gradient_as_bucket_view=True,
+                bucket_cap_mb=bucket_cap_mb,
+                broadcast_buffers=False,
+            )
+        else:
+            self.engine = self.model
+        self.opt = torch.optim.AdamW(
+            self.model.parameters(), lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=weight_decay,
+            fused=device.type == "cuda",
+        )
+
+    def step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """One optimizer step over this rank's ``[B, T]`` batch; returns the mean loss (device scalar,
+        no host synchronisation)."""
+        n = input_ids.shape[0]
+        chunks = max(1, (n + self.micro_batch - 1) // self.micro_batch)
+        total = torch.zeros((), device=input_ids.device, dtype=torch.float32)
+        for i in range(chunks):
+            lo = i * self.micro_batch
+            hi = min(n, lo + self.micro_batch)
+            frac = (hi - lo) / n
+            sync_ctx = self.engine.no_sync() if (self.world > 1 and i < chunks - 1) else contextlib.nullcontext()
+            with sync_ctx:
+                loss = self.engine(input_ids[lo:hi], labels[lo:hi])
+                (loss * frac).backward()
+            total += loss.detach() * frac
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=self.world == 1)
+        return total

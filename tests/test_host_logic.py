@@ -1,0 +1,89 @@
+"""Host-side logic that needs no GPU: operator validation and error behaviour,
+the synthetic token stream, FLOP accounting, the bench contract helpers."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+
+def test_ops_refuse_cpu_tensors_instead_of_falling_back():
+    from mega_trading_b200.kernels import triton_attention as A
+    from mega_trading_b200.kernels import triton_ops as K
+
+    x = torch.randn(2, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.triton_rms_norm(x, torch.ones(8), eps=1e-5)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.triton_swiglu_gate(x, x)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.triton_add_rms_norm(x, x, torch.ones(8), eps=1e-5)
+    q = torch.randn(1, 4, 8, 32)
+    with pytest.raises(RuntimeError, match="requires CUDA tensors"):
+        A.triton_attention(q, q[:, :2], q[:, :2], repeats=2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.triton_apply_rope(q, q, torch.ones(8, 16), torch.ones(8, 16))
+
+
+def test_validation_messages_match_reference():
+    from mega_trading_b200.kernels import triton_ops as K
+
+    h = torch.randn(4, 8)
+    w = torch.randn(11, 8)
+    lab = torch.zeros(4, dtype=torch.long)
+    with pytest.raises(ValueError, match="hidden must have shape"):
+        K.triton_fused_linear_cross_entropy(h[None], w, lab)
+    with pytest.raises(ValueError, match="weight must have shape"):
+        K.triton_fused_linear_cross_entropy(h, w[:, :4], lab)
+    with pytest.raises(ValueError, match="labels must be a 1D tensor"):
+        K.triton_fused_linear_cross_entropy(h, w, lab[None])
+    with pytest.raises(ValueError, match="labels must be an integer tensor"):
+        K.triton_fused_linear_cross_entropy(h, w, lab.float())
+
+
+def test_composite_tokens_distribution():
+    from mega_trading_b200.data import VOCAB_SIZE, _ZIPF, composite_tokens, next_token_batch
+
+    t = composite_tokens(64, 512, seed=1)
+    assert t.dtype == torch.int64 and t.min() >= 0 and t.max() < VOCAB_SIZE == 21504
+    dt = t % 16
+    vol = (t // 16) % 16
+    depth = (t // 256) % 21
+    side = (t // (256 * 21)) % 2
+    action = t // (256 * 21 * 2)
+    assert action.max() <= 1
+    for field in (dt, vol):
+        freq = torch.bincount(field.flatten(), minlength=16).double() / field.numel()
+        assert torch.allclose(freq, _ZIPF, atol=6e-3)
+    # geometric(p=0.3) - 1: P(0) = 0.3
+    assert abs(float((depth == 0).double().mean()) - 0.3) < 6e-3
+    assert abs(float(side.double().mean()) - 0.5) < 6e-3
+    ids, labels = next_token_batch(2, 16, seed=9)
+    full = composite_tokens(2, 17, seed=9)
+    assert torch.equal(ids, full[:, :-1]) and torch.equal(labels, full[:, 1:])
+    assert torch.equal(composite_tokens(3, 5, seed=4), composite_tokens(3, 5, seed=4))
+
+
+def test_flop_accounting_matches_survey():
+    from mega_trading_b200.model import CONFIGS
+
+    cfg = CONFIGS["gqa12"]
+    assert cfg.matmul_params() == 92_012_544
+    per_tok = cfg.train_flops_per_token(2048)
+    assert math.isclose(per_tok, 684.3e6, rel_tol=2e-3)
+    assert math.isclose(per_tok * 256 * 2048, 358.8e12, rel_tol=2e-3)
+    big = CONFIGS["large24"]
+    assert math.isclose(big.train_flops_per_token(4096), 2.460e9, rel_tol=2e-3)
+
+
+def test_clock_sampler_summary_parses_nvidia_smi_rows(tmp_path):
+    import bench
+
+    s = bench.ClockSampler(0)
+    s.path = tmp_path / "c.csv"
+    s.path.write_text("0, 1965, 1965, 700.5, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+                      "0, 1800, 1965, 990.1, 0x4, Not Active, Not Active, Not Active, Active\n")
+    out = s.summary()
+    assert out["sm_max_mhz"] == 1965.0 and out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
