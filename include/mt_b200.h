@@ -86,6 +86,25 @@ MT_API int mt_rms_norm_bwd(const void* x, int x_dtype, const void* w, int w_dtyp
                     int64_t workspace_bytes, int64_t rows, int64_t dim,
                     void* stream);
 
+/* RMSNorm backward for callers that cannot allocate device memory where they
+ * call it.  No counterpart in the reference: it exists for hosts that bind this
+ * C ABI without a device allocator of their own at the call site (an FFI
+ * caller, or code running while another runtime owns the device memory
+ * pool), and for code that must not call cudaMalloc/cudaFree in its step
+ * because they synchronise the device.  Same math and arguments as
+ * mt_rms_norm_bwd minus the workspace: the dW partials live in a 4 MiB
+ * static device array inside the library (held by every GPU that loads it).
+ * Limits: dim <= 4096 (larger returns MT_ERR_WORKSPACE).  The first call on a
+ * device looks up the array's device address; make that first call before any
+ * stream capture.  All calls on a device share the array and it keeps the
+ * last call's contents (each call overwrites what it reads), so two calls that
+ * can run at the same time on one device, e.g. on two streams, race: order
+ * them on one stream. */
+MT_API int mt_rms_norm_bwd_noalloc(const void* x, int x_dtype, const void* w, int w_dtype,
+                                   const float* rstd, const void* dy, int dy_dtype, void* dx,
+                                   int dx_dtype, void* dw, int dw_dtype, int64_t rows,
+                                   int64_t dim, void* stream);
+
 /* ---------------------------------------------------------------------
  * Fused residual add + RMSNorm   replaces triton_add_rms_norm
  *   (src/mega_trading/kernels/triton_ops.py:18-42, forward kernel :541-566,

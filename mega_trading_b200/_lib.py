@@ -36,6 +36,10 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp],
     ),
+    "mt_rms_norm_bwd_noalloc": (
+        c_int,
+        [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_i64, c_i64, c_vp],
+    ),
     "mt_add_rms_norm_fwd": (
         c_int,
         [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64, c_float, c_vp],

@@ -17,6 +17,8 @@ void set_last_error(const char* where, cudaError_t err) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(err), cudaGetErrorString(err));
 }
 
+void set_last_error_text(const char* text) { snprintf(g_last_error, sizeof(g_last_error), "%s", text); }
+
 int check_launch(const char* where) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {

@@ -16,6 +16,7 @@ namespace mt {
 // host-side status helpers (defined in capi.cu)
 // ---------------------------------------------------------------------------
 void set_last_error(const char* where, cudaError_t err);
+void set_last_error_text(const char* text);
 int check_launch(const char* where);
 int check_arch();  // MT_OK on sm_100, MT_ERR_UNSUPPORTED_ARCH otherwise
 // Make the primary context of the device that owns `ptr` current on this

@@ -12,6 +12,8 @@
 // visits, reduces the 8 warps of a block through shared memory and writes one
 // fp32 partial row per block into the caller's workspace; a second small
 // kernel sums the partials in a fixed order (deterministic dW).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mt {
@@ -304,8 +306,10 @@ int bwd_blocks(int64_t rows) {
 
 template <bool GRES, typename TX, typename TW, typename TG, typename TGR, typename TD, typename TDW>
 int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* gres, void* dx, void* dw,
-               void* workspace, int64_t ws_bytes, int64_t rows, int64_t dim, cudaStream_t stream) {
-  const int nblocks = bwd_blocks(rows);
+               void* workspace, int64_t ws_bytes, int64_t rows, int64_t dim, cudaStream_t stream,
+               int max_blocks = 0) {
+  int nblocks = bwd_blocks(rows);
+  if (max_blocks > 0 && nblocks > max_blocks) nblocks = max_blocks;
   if (workspace == nullptr || ws_bytes < int64_t(nblocks) * dim * 4) return MT_ERR_WORKSPACE;
   float* partial = static_cast<float*>(workspace);
   const int nc = chunks_for(dim);
@@ -471,3 +475,88 @@ int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// RMSNorm backward without caller-provided scratch.
+//
+// For callers that cannot allocate device memory at the call site, the dW
+// partial sums live in this file-scope device array instead of a workspace.
+// Its capacity bounds the launch: at most kNoAllocBlocks blocks of per-block
+// partial rows of at most kNoAllocMaxDim floats (4 MiB, held by every GPU that
+// loads the library until the process exits).  Every block overwrites its own
+// partial row completely before the second stage reads it, so nothing has to
+// be cleared between calls; two calls that overlap on the GPU would share the
+// array and race.
+// ---------------------------------------------------------------------------
+namespace mt {
+namespace {
+
+constexpr int kNoAllocBlocks = 256;
+constexpr int kNoAllocMaxDim = 4096;
+
+static __device__ __align__(256) float g_rms_bwd_noalloc_partial[kNoAllocBlocks * kNoAllocMaxDim];
+
+constexpr int kMaxNoAllocDevices = 64;
+float* g_noalloc_addr[kMaxNoAllocDevices];
+std::mutex g_noalloc_mutex;
+
+// The array's name is only a host-side stand-in; the kernels need the device
+// address, looked up once per device with that device current.
+int noalloc_scratch(const void* any_device_ptr, float** out) {
+  int st = bind_device_of(any_device_ptr);
+  if (st != MT_OK) return st;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    set_last_error("cudaGetDevice", err);
+    return MT_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kMaxNoAllocDevices) return MT_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_rms_bwd_noalloc_partial);
+    if (err != cudaSuccess || ptr == nullptr) {
+      set_last_error("cudaGetSymbolAddress(rms_norm_bwd no-alloc scratch)", err);
+      return MT_ERR_LAUNCH;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_addr[dev];
+  return MT_OK;
+}
+
+}  // namespace
+}  // namespace mt
+
+extern "C" int mt_rms_norm_bwd_noalloc(const void* x, int x_dtype, const void* w, int w_dtype, const float* rstd,
+                                       const void* dy, int dy_dtype, void* dx, int dx_dtype, void* dw, int dw_dtype,
+                                       int64_t rows, int64_t dim, void* stream) {
+  int st = validate_rows(x, dx, rows, dim);
+  if (st != MT_OK) return st;
+  if (dim > kNoAllocMaxDim) {
+    mt::set_last_error_text("mt_rms_norm_bwd_noalloc: dim exceeds the built-in scratch limit of 4096");
+    return MT_ERR_WORKSPACE;
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) return zero_dw(dw, dw_dtype, dim, s);
+  float* scratch = nullptr;
+  if ((st = noalloc_scratch(x, &scratch)) != MT_OK) return st;
+  const int64_t cap_bytes = int64_t(kNoAllocBlocks) * kNoAllocMaxDim * 4;
+  using bf = __nv_bfloat16;
+  using hf = __half;
+  switch (key5(x_dtype, w_dtype, dy_dtype, dx_dtype, dw_dtype)) {
+#define CASE(a, b, c, d, e, TA, TB, TC, TD, TE)                                                                   \
+  case key5(a, b, c, d, e):                                                                                        \
+    return launch_bwd<false, TA, TB, TC, TC, TD, TE>(x, w, rstd, dy, nullptr, dx, dw, scratch, cap_bytes, rows, dim, \
+                                                     s, kNoAllocBlocks);
+    CASE(MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, bf, bf, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, hf, hf, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, float, float, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, MT_BF16, MT_F32, bf, float, bf, bf, float)
+    CASE(MT_F16, MT_F32, MT_F16, MT_F16, MT_F32, hf, float, hf, hf, float)
+    CASE(MT_F32, MT_F32, MT_BF16, MT_F32, MT_F32, float, float, bf, float, float)
+#undef CASE
+    default: return MT_ERR_UNSUPPORTED_DTYPE;
+  }
+}
