@@ -1,0 +1,224 @@
+"""Per-operator microbenchmarks at the BASELINE operator shapes.
+
+``python -m mega_trading_b200.microbench [--ops attention,ce,rmsnorm,rope,swiglu] [--iters N]``
+
+* attention: config 1 -- B=16, Hq=16, Hkv=4, D=64, T in {1024, 2048, 4096},
+  q/k/v ~ N(0,1)*0.5, dO ~ N(0,1), forward and backward, TFLOP/s with the
+  reference's causal FLOP count (``scripts/benchmark_triton_attention.py:179-190``:
+  4*B*Hq*D*T(T+1)/2 forward; backward 2.5x forward).
+* ce: config 2 -- N=65,536 rows, hidden 768, vocab 21,504; forward
+  (2NHV FLOP) and the logit-gradient kernel (2NHV FLOP).
+* rmsnorm / rope / swiglu: config 2 token count, HBM GB/s of the algorithmic
+  bytes (each input read once, each output written once).
+
+Times are CUDA-event means on the launching stream after warm-up; inputs are
+regenerated per case and exceed L2 except where noted.  ``--profile`` runs
+each selected case ``--iters`` times without timing (for an ncu capture).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from . import _lib
+from .kernels import triton_attention as A
+from .kernels import triton_ops as K
+from .kernels.fused_ce import _FusedLinearCrossEntropy  # noqa: F401  (autograd path used below)
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def _time(fn, iters: int, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def attention_cases(dev, iters, profile, seqs=(1024, 2048, 4096), batch=16):
+    out = []
+    for T in seqs:
+        B, Hq, Hkv, D = batch, 16, 4, 64
+        g = torch.Generator(device=dev).manual_seed(T)
+        q = (torch.randn(B, Hq, T, D, device=dev, generator=g) * 0.5).bfloat16()
+        k = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16()
+        v = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16()
+        do = torch.randn(B, Hq, T, D, device=dev, generator=g).bfloat16()
+        scale = 1.0 / math.sqrt(D)
+        o, lse = A._launch_fwd(q, k, v, Hq // Hkv, scale)
+        fwd = lambda: A._launch_fwd(q, k, v, Hq // Hkv, scale)  # noqa: E731
+        bwd = lambda: A._launch_bwd(q, k, v, o, lse, do, scale)  # noqa: E731
+        if profile:
+            for _ in range(iters):
+                fwd()
+                bwd()
+            continue
+        flops = 4.0 * B * Hq * D * T * (T + 1) / 2
+        ms_f = _time(fwd, iters)
+        ms_b = _time(bwd, iters)
+        out.append({"op": "attention", "T": T, "B": B, "fwd_ms": ms_f, "fwd_tflops": flops / ms_f / 1e9,
+                    "bwd_ms": ms_b, "bwd_tflops": 2.5 * flops / ms_b / 1e9,
+                    "fwd_bwd_tflops": 3.5 * flops / (ms_f + ms_b) / 1e9})
+    return out
+
+
+def ce_cases(dev, iters, profile, n=65536, h=768, v=21504):
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(5)
+    hid = (torch.randn(n, h, device=dev, generator=g) * 0.5).bfloat16()
+    w = (torch.randn(v, h, device=dev, generator=g) * 0.02).bfloat16()
+    lab = torch.randint(0, v, (n,), device=dev, generator=g)
+    loss = torch.empty((), device=dev)
+    lse2 = torch.empty(n + 3, device=dev)
+    ws = torch.empty(int(lib.mt_fused_ce_workspace_bytes(n, v)), device=dev, dtype=torch.uint8)
+    dz = torch.empty(n, v, device=dev, dtype=torch.bfloat16)
+    one = torch.ones(1, device=dev)
+    status = _lib.status_word(dev)
+    stream = _lib.stream_ptr(dev)
+
+    def fwd():
+        _lib.check(lib.mt_fused_ce_fwd(hid.data_ptr(), w.data_ptr(), lab.data_ptr(), 1, -100, 2, n, v, h,
+                                       loss.data_ptr(), lse2.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       status.data_ptr(), stream), "ce fwd")
+
+    def grad():
+        _lib.check(lib.mt_fused_ce_grad_logits(hid.data_ptr(), w.data_ptr(), lab.data_ptr(), 1, -100, 2, n, v, h,
+                                               lse2.data_ptr(), one.data_ptr(), dz.data_ptr(), v,
+                                               status.data_ptr(), stream), "ce grad")
+
+    fwd()
+    if profile:
+        for _ in range(iters):
+            fwd()
+            grad()
+        return []
+    flops = 2.0 * n * h * v
+    ms_f = _time(fwd, iters)
+    ms_g = _time(grad, iters)
+    return [{"op": "fused_ce", "N": n, "H": h, "V": v, "fwd_ms": ms_f, "fwd_tflops": flops / ms_f / 1e9,
+             "grad_logits_ms": ms_g, "grad_logits_tflops": flops / ms_g / 1e9,
+             "grad_logits_bytes_written": n * v * 2}]
+
+
+def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65536):
+    out = []
+    g = torch.Generator(device=dev).manual_seed(9)
+    if "rmsnorm" in ops:
+        H = 768
+        x = torch.randn(n, H, device=dev, generator=g).bfloat16()
+        w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).bfloat16()
+        dy = torch.randn(n, H, device=dev, generator=g).bfloat16()
+        y, rstd = K._rms_fwd(x, w, 1e-5, torch.bfloat16)
+        f = lambda: K._rms_fwd(x, w, 1e-5, torch.bfloat16)  # noqa: E731
+        b = lambda: K._rms_bwd(x, w, rstd, dy, torch.bfloat16)  # noqa: E731
+        if profile:
+            for _ in range(iters):
+                f()
+                b()
+        else:
+            bf, bb = 2 * n * H * 2 + 4 * n, 3 * n * H * 2 + 4 * n
+            mf, mb = _time(f, iters), _time(b, iters)
+            out.append({"op": "rms_norm", "N": n, "H": H, "fwd_ms": mf, "fwd_gbs": bf / mf / 1e6, "bwd_ms": mb,
+                        "bwd_gbs": bb / mb / 1e6})
+    if "rope" in ops:
+        B, T, D = n // 2048, 2048, 64
+        q = torch.randn(B, T, 12, D, device=dev, generator=g).bfloat16().transpose(1, 2)
+        k = torch.randn(B, T, 4, D, device=dev, generator=g).bfloat16().transpose(1, 2)
+        pos = torch.arange(T, device=dev, dtype=torch.float32)
+        inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+        fr = torch.outer(pos, inv)
+        cos, sin = fr.cos().bfloat16(), fr.sin().bfloat16()
+        qo, ko = torch.empty_like(q), torch.empty_like(k)
+        f = lambda: K._launch_rope(q, k, cos, sin, qo, ko, negate=False)  # noqa: E731
+        if profile:
+            for _ in range(iters):
+                f()
+        else:
+            byts = 2 * n * 16 * D * 2
+            m = _time(f, iters)
+            out.append({"op": "rope", "N": n, "heads": "12+4", "D": D, "ms": m, "gbs": byts / m / 1e6})
+    if "swiglu" in ops:
+        I = 2048
+        gt = torch.randn(n, I, device=dev, generator=g).bfloat16()
+        up = torch.randn(n, I, device=dev, generator=g).bfloat16()
+        dy = torch.randn(n, I, device=dev, generator=g).bfloat16()
+        lib = _lib.load()
+        y, dg, du = torch.empty_like(gt), torch.empty_like(gt), torch.empty_like(gt)
+        st = _lib.stream_ptr(dev)
+        f = lambda: lib.mt_swiglu_fwd(gt.data_ptr(), up.data_ptr(), y.data_ptr(), 2, gt.numel(), st)  # noqa: E731
+        b = lambda: lib.mt_swiglu_bwd(gt.data_ptr(), up.data_ptr(), dy.data_ptr(), dg.data_ptr(),  # noqa: E731
+                                      du.data_ptr(), 2, gt.numel(), st)
+        if profile:
+            for _ in range(iters):
+                f()
+                b()
+        else:
+            mf, mb = _time(f, iters), _time(b, iters)
+            out.append({"op": "swiglu", "N": n, "I": I, "fwd_ms": mf, "fwd_gbs": 3 * n * I * 2 / mf / 1e6,
+                        "bwd_ms": mb, "bwd_gbs": 5 * n * I * 2 / mb / 1e6})
+    return out
+
+
+def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0, attn_seqs=(1024, 2048, 4096),
+        attn_batch: int = 16, ce_rows: int = 65536) -> list[dict]:
+    dev = torch.device("cuda", device)
+    torch.cuda.set_device(dev)
+    res: list[dict] = []
+    if "attention" in ops:
+        res += attention_cases(dev, iters, profile, attn_seqs, attn_batch)
+    if "ce" in ops:
+        res += ce_cases(dev, iters, profile, n=ce_rows)
+    bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
+    if bw:
+        res += bandwidth_cases(dev, iters, profile, tuple(bw))
+    torch.cuda.synchronize()
+    status = _lib.read_status(dev)
+    if status:
+        raise RuntimeError(f"device status word {status:#x}")
+    peaks = _peaks()
+    for r in res:
+        for key in list(r):
+            if key.endswith("tflops"):
+                r[key.replace("tflops", "frac")] = r[key] / peaks["bf16_tflops"]
+            if key.endswith("gbs"):
+                r[key.replace("gbs", "frac")] = r[key] / peaks["hbm_gbs"]
+    return res
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--ops", default="attention,ce,rmsnorm,rope,swiglu")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--profile", action="store_true")
+    ap.add_argument("--seqs", default="1024,2048,4096")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--ce-rows", type=int, default=65536)
+    args = ap.parse_args(argv)
+    res = run(args.ops.split(","), args.iters, args.profile, attn_seqs=tuple(int(s) for s in args.seqs.split(",")),
+              attn_batch=args.batch, ce_rows=args.ce_rows)
+    for r in res:
+        print(json.dumps(r))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
