@@ -20,9 +20,10 @@
 //         dV  += P^T dO       cols [256,256+D)    (accumulated over the group)
 //         dK  += dS^T Q       cols [256+D,256+2D)
 //         dQ   = dS K         cols [256+2D,256+3D) (M=128 queries)
-//     P^T and dS^T are written once, bf16/fp16, to 128B-swizzled shared
-//     tiles; dS^T serves as the K-major A operand of dK and, read MN-major,
-//     as the A operand of dQ.  Q, dO and K are consumed MN-major where they
+//     P^T is stored (bf16/fp16 pairs) into TMEM columns [448,512) and dV
+//     reads it as a TMEM A operand; dS^T is written once to a 128B-swizzled
+//     shared tile that serves as the K-major A operand of dK and, read
+//     MN-major, as the A operand of dQ.  Q, dO and K are consumed MN-major where they
 //     act as B of a key-contracted product, so nothing is transposed.
 //   * dQ partials leave the CTA through a TMA bulk tensor reduce-add (fp32)
 //     from a 128B-swizzled staging tile; dK/dV never leave TMEM until the
@@ -63,8 +64,7 @@ struct BwdCfg {
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_Q = OFF_V + TILE;
   static constexpr int OFF_DO = OFF_Q + kNQ * TILE;
-  static constexpr int OFF_P = OFF_DO + kNQ * TILE;
-  static constexpr int OFF_DS = OFF_P + PT_BYTES;
+  static constexpr int OFF_DS = OFF_DO + kNQ * TILE;
   static constexpr int OFF_DQ = OFF_DS + PT_BYTES;
   static constexpr int OFF_LSE = OFF_DQ + DQ_BYTES;      // [kNQ][128] fp32
   static constexpr int OFF_DELTA = OFF_LSE + kNQ * 512;  // [kNQ][128] fp32
@@ -72,6 +72,7 @@ struct BwdCfg {
   static constexpr int SMEM = OFF_BAR + 256;
   static constexpr int TMEM_COLS = 512;
   static constexpr int T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D, T_DQ = 256 + 2 * D;
+  static constexpr int T_PT = 448;  // P^T, 16-bit pairs: A operand of dV += P^T dO
 };
 
 struct BwdParams {
@@ -133,7 +134,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
   uint8_t* sV = smem + C::OFF_V;
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sDO = smem + C::OFF_DO;
-  uint8_t* sP = smem + C::OFF_P;
   uint8_t* sDS = smem + C::OFF_DS;
   uint8_t* sDQ = smem + C::OFF_DQ;
   float* sLse = reinterpret_cast<float*>(smem + C::OFF_LSE);
@@ -224,16 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       constexpr uint32_t idesc_dq = make_idesc(128, D, kBf16, 1, 1);    // A and B MN-major
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
-      const uint32_t p_base = smem_u32(sP), ds_base = smem_u32(sDS);
-      bool ok = wait_bounded(wc, bar_kv, 0, 2);
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int st = it % kNQ;
-        if (!wait_bounded(wc, &bar_q_full[st], (it / kNQ) & 1, 3) ||
-            (it > 0 && !wait_bounded(wc, bar_sd_free, (it - 1) & 1, 4))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      const uint32_t ds_base = smem_u32(sDS);
+      auto issue_sdp = [&](int st) {
         const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -246,19 +238,44 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
                   make_sdesc(dob + kk * 32, 16, C::SBO, C::LAYOUT), idesc_sd, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar_sd_full);
+      };
+      // Issue order per tile i: S/dP of tile i+1 as soon as the compute warps
+      // have read S/dP of tile i, then dV, dK, dQ of tile i -- so the compute
+      // warps' softmax of tile i+1 overlaps the three accumulating products.
+      bool ok = wait_bounded(wc, bar_kv, 0, 2) && wait_bounded(wc, &bar_q_full[0], 0, 3);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0);
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % kNQ;
+        if (!wait_bounded(wc, bar_sd_free, it & 1, 4)) {
+          ok = false;
+          break;
+        }
+        if (it + 1 < n_it) {
+          const int st1 = (it + 1) % kNQ;
+          if (!wait_bounded(wc, &bar_q_full[st1], ((it + 1) / kNQ) & 1, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_sdp(st1);
+        }
         if (!wait_bounded(wc, bar_pds_full, it & 1, 5)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
         // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
 #pragma unroll
         for (int kk = 0; kk < kBQ / 16; ++kk) {
           const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
           const uint32_t b_off = kk * 16 * C::ROW_BYTES;
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_ss(tmem + C::T_DV, make_sdesc(p_base + a_off, 16, 1024, kSwizzle128),
-                  make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
+          umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),
+                  idesc_acc, acc);
           umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
                   make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
         }
@@ -288,6 +305,55 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const int key = kt * kBK + r;
     bool ok = true;
+    // Drain dQ of tile `pit` (query head ph, query tile pq): TMEM -> swizzled
+    // fp32 staging -> TMA reduce-add into the accumulator.  Returns false on abort.
+    auto drain_dq = [&](int pit, int ph, int pq) -> bool {
+      if (!bar_all(wait_bounded(wc, bar_dq_full, pit & 1, 9), 4, 256)) return false;
+      tc_fence_after();
+      constexpr int kCols = D / 2;  // dQ columns per warpgroup
+      const bool leader = (threadIdx.x & 127) == 0;
+      // the previous reduce of this warpgroup must have finished reading staging
+      if (leader) bulk_wait_group_read0();
+      named_bar_sync(1 + wg, 128);
+      // 16 columns at a time: TMEM -> registers -> fp32 staging (box bx = 32
+      // columns x 128 rows, 128 B rows, 128B swizzle)
+#pragma unroll
+      for (int half = 0; half < kCols / 16; ++half) {
+        uint32_t qv[16];
+        tmem_ld16(tmem + lane_off + C::T_DQ + wg * kCols + half * 16, qv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int col = wg * kCols + half * 16 + q * 4;
+          const int bx = col >> 5;
+          const int ch = (col & 31) >> 2;
+          *reinterpret_cast<uint4*>(sDQ + bx * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16)) =
+              make_uint4(qv[q * 4], qv[q * 4 + 1], qv[q * 4 + 2], qv[q * 4 + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_dq_free);
+      fence_proxy_async_smem();
+      const int row0 = (b * p.Hq + ph) * p.Tp + pq * kBQ;
+      if constexpr (kCols == 32) {
+        named_bar_sync(1 + wg, 128);
+        if (leader) {
+          tma_reduce_add_2d(&p.tm_dq, sDQ + wg * (128 * 128), wg * 32, row0);
+          bulk_commit_group();
+        }
+      } else {
+        // D == 32: both halves live in box 0; one thread issues after both wrote
+        named_bar_sync(3, 256);
+        if (threadIdx.x == 0) {
+          tma_reduce_add_2d(&p.tm_dq, sDQ, 0, row0);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+        }
+        named_bar_sync(3, 256);
+      }
+      return true;
+    };
+    int prev_h = 0, prev_q = 0;
     for (int it = 0; it < n_it; ++it) {
       const int st = it % kNQ;
       const int rr = it / n_q;
@@ -301,87 +367,61 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       tc_fence_after();
       const float* lse = sLse + st * 128;
       const float* dl = sDelta + st * 128;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = wg * 64 + c * 32;
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tmem + lane_off + C::T_S + col0, sv);
-        tmem_ld32(tmem + lane_off + C::T_DP + col0, dv);
-        tmem_ld_wait();
-        float pv[32], dsv[32];
+      // P^T and dS^T rows for this warpgroup's 64 query columns, packed in
+      // registers until the previous tile's products have released the tiles
+      uint32_t pk[2][16], dk[2][16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int q = qi * kBQ + col0 + i;
-          float pp = fast_exp2(__uint_as_float(sv[i]) * p.scale_log2 - lse[col0 + i]);
-          if (diag && key > q) pp = 0.f;
-          pv[i] = pp;
-          dsv[i] = pp * (__uint_as_float(dv[i]) - dl[col0 + i]);
+      for (int c = 0; c < 4; ++c) {
+        const int col0 = wg * 64 + c * 16;
+        uint32_t sv[16], dv[16];
+        tmem_ld16(tmem + lane_off + C::T_S + col0, sv);
+        tmem_ld16(tmem + lane_off + C::T_DP + col0, dv);
+        tmem_ld_wait();
+        const int lim = key - (qi * kBQ + col0);  // column i is masked when i < lim (key > query)
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          float p0 = fast_exp2(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse[col0 + i]));
+          float p1 = fast_exp2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -lse[col0 + i + 1]));
+          if (diag) {
+            if (i < lim) p0 = 0.f;
+            if (i + 1 < lim) p1 = 0.f;
+          }
+          const float d0 = p0 * (__uint_as_float(dv[i]) - dl[col0 + i]);
+          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dl[col0 + i + 1]);
+          pk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
+          dk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(d0, d1);
         }
-        store_row32<T>(sP, r, col0, pv);
-        store_row32<T>(sDS, r, col0, dsv);
       }
       tc_fence_before();
       mbar_arrive(bar_sd_free);
-      fence_proxy_async_smem();
-      mbar_arrive(bar_pds_full);
-
-      // drain dQ of this tile: TMEM -> swizzled fp32 staging -> TMA reduce-add
-      if (!bar_all(wait_bounded(wc, bar_dq_full, it & 1, 9), 4, 256)) {
+      // dV/dK/dQ of the previous tile are complete once its dQ is: then the
+      // P/dS tiles are free and its dQ can be drained
+      if (it > 0 && !drain_dq(it - 1, prev_h, prev_q)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      constexpr int kCols = D / 2;  // dQ columns per warpgroup
-      uint32_t qv[kCols];
-      if constexpr (kCols == 32) {
-        tmem_ld32(tmem + lane_off + C::T_DQ + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(qv));
-      } else {
-        tmem_ld16(tmem + lane_off + C::T_DQ + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(qv));
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(bar_dq_free);
-      const bool leader = (threadIdx.x & 127) == 0;
-      // the previous reduce of this warpgroup must have finished reading staging
-      if (leader) bulk_wait_group_read0();
-      named_bar_sync(1 + wg, 128);
-      {
-        // fp32 staging: box bx = 32 columns x 128 rows, 128 B rows, 128B swizzle
-        const int colbase = wg * kCols;
+      // P^T rows -> TMEM (this warpgroup's 64 query columns = 32 packed columns)
+      tmem_st16(tmem + lane_off + C::T_PT + wg * 32, pk[0]);
+      tmem_st16(tmem + lane_off + C::T_PT + wg * 32 + 16, pk[1]);
 #pragma unroll
-        for (int q = 0; q < kCols / 4; ++q) {
-          const int col = colbase + q * 4;
-          const int bx = col >> 5;
-          const int ch = (col & 31) >> 2;
-          uint4 w;
-          w.x = qv[q * 4 + 0];
-          w.y = qv[q * 4 + 1];
-          w.z = qv[q * 4 + 2];
-          w.w = qv[q * 4 + 3];
-          *reinterpret_cast<uint4*>(sDQ + bx * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16)) = w;
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = wg * 64 + c * 32;
+        uint8_t* db = sDS + (col0 >> 6) * (128 * 128) + r * 128;
+        const int ch0 = (col0 & 63) >> 3;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int off = ((ch0 + q) ^ (r & 7)) * 16;
+          *reinterpret_cast<uint4*>(db + off) = make_uint4(dk[c][q * 4], dk[c][q * 4 + 1], dk[c][q * 4 + 2], dk[c][q * 4 + 3]);
         }
       }
+      tmem_st_wait();
+      tc_fence_before();
       fence_proxy_async_smem();
-      named_bar_sync(1 + wg, 128);
-      if (leader) {
-        const int row0 = (b * p.Hq + h) * p.Tp + qi * kBQ;
-        if constexpr (kCols == 32) {
-          tma_reduce_add_2d(&p.tm_dq, sDQ + wg * (128 * 128), wg * 32, row0);
-          bulk_commit_group();
-        } else if (wg == 1) {
-          // D == 32: both halves live in box 0; warpgroup 1 issues after both wrote
-        }
-      }
-      if constexpr (kCols != 32) {
-        named_bar_sync(3, 256);
-        if (threadIdx.x == 0) {
-          tma_reduce_add_2d(&p.tm_dq, sDQ, 0, (b * p.Hq + h) * p.Tp + qi * kBQ);
-          bulk_commit_group();
-          bulk_wait_group_read0();
-        }
-        named_bar_sync(3, 256);
-      }
+      mbar_arrive(bar_pds_full);
+      prev_h = h;
+      prev_q = qi;
     }
+    if (ok && n_it > 0 && !drain_dq(n_it - 1, prev_h, prev_q)) ok = false;
     // final: dV and dK (scaled) for this key tile
     if (ok && bar_all(wait_bounded(wc, bar_done, 0, 10), 4, 256)) {
       tc_fence_after();

@@ -9,19 +9,22 @@
 //
 // B200 design
 //   * One CTA = two consecutive 128-row query tiles ("slots") of one
-//     (batch, query head); both slots share one K/V tile stream.  One CTA
-//     per SM (160 KB smem, all 512 TMEM columns).
+//     (batch, query head); both slots share one K/V tile stream (3 stages).
+//     One CTA per SM (128 KB smem, all 512 TMEM columns).
 //   * Warp roles: warps 0-3 / 4-7 = softmax of slot 0 / 1 (thread i owns TMEM
 //     lane = query row i of its slot), warp 8 = TMA producer (+ TMEM
 //     allocation), warp 9 = tcgen05.mma issuer.
 //   * Per slot s: S = Q K^T (M=128, N=128, K=D) accumulates in TMEM columns
-//     [256s, 256s+128); O += P V (M=128, N=D, K=128) in [256s+128, 256s+128+D).
+//     [256s, 256s+128); O += P V (M=128, N=D, K=128) in [256s+128, 256s+128+D);
+//     P lives in [256s+192, 256s+256).
 //   * Q/K/V tiles arrive by TMA (no multicast) in the 128B (D=64) or 64B (D=32)
 //     swizzle that the UMMA shared-memory descriptors expect; V is consumed
 //     MN-major so it needs no transpose.  K/V are double-buffered.
 //   * P is rounded to the input dtype (as the reference does before its PV
-//     dot, triton_attention.py:340) and written to a 128B-swizzled K-major
-//     shared tile for the PV MMA.
+//     dot, triton_attention.py:340) and stored into TMEM next to S and O; the
+//     P V product reads it from TMEM (tcgen05.mma with a TMEM A operand), so
+//     only V is read from shared memory (shared-memory bandwidth, not the
+//     tensor core, limits an all-shared-memory P V at N = D = 64).
 //   * Causal: key tiles 0..qtile only; the diagonal tile is masked in
 //     registers.  CTAs are launched heaviest query tile first.
 //   * Every mbarrier wait is bounded (status word + early exit, no trap).
@@ -45,15 +48,16 @@ struct FwdCfg {
   static constexpr uint32_t LAYOUT = (D == 64) ? kSwizzle128 : kSwizzle64;
   static constexpr int SBO = 8 * ROW_BYTES;  // bytes between 8-row core groups
   static constexpr int TILE = kBM * ROW_BYTES;
-  static constexpr int NST = 2;
-  static constexpr int P_BYTES = kBM * kBN * 2;
+  static constexpr int NST = 3;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + kSlots * TILE;
   static constexpr int OFF_V = OFF_K + NST * TILE;
-  static constexpr int OFF_P = OFF_V + NST * TILE;
-  static constexpr int OFF_BAR = OFF_P + kSlots * P_BYTES;
+  static constexpr int OFF_BAR = OFF_V + NST * TILE;
   static constexpr int SMEM = OFF_BAR + 512;
-  static constexpr int TMEM_COLS = 512;  // slot s: S at 256*s, O at 256*s + 128
+  // TMEM per slot s (256 columns): S fp32 [0,128), O fp32 [128,128+D),
+  // P (bf16/fp16 pairs, the A operand of P V) [192,256)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int T_O = 128, T_P = 192;
 };
 
 struct FwdParams {
@@ -88,7 +92,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sK = smem + C::OFF_K;
   uint8_t* sV = smem + C::OFF_V;
-  uint8_t* sP = smem + C::OFF_P;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* bar_q = bars + 0;                    // [kSlots]
   uint64_t* bar_k_full = bars + 2;               // [NST]
@@ -177,7 +180,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t k_base = smem_u32(sK);
       const uint32_t v_base = smem_u32(sV);
-      const uint32_t p_base = smem_u32(sP);
       auto issue_s = [&](int slot, int st) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -187,12 +189,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
       };
       auto issue_pv = [&](int slot, int st, bool acc_first) {
+        // A = P from TMEM (16 keys = 8 packed columns per step), B = V (MN-major)
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t ad = make_sdesc(p_base + slot * C::P_BYTES + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16,
-                                         1024, kSwizzle128);
           const uint64_t bd = make_sdesc(v_base + st * C::TILE + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT);
-          umma_ss(tmem + slot * 256 + 128, ad, bd, idesc_o, (acc_first || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + slot * 256 + C::T_O, tmem + slot * 256 + C::T_P + kk * 8, bd, idesc_o,
+                  (acc_first || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = wait_bounded(wc, &bar_q[0], 0, 2) && (!active1 || wait_bounded(wc, &bar_q[1], 0, 2)) &&
@@ -251,12 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     const int qrow = qt * kBM + r;
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + slot * 256 + lane_off;
-    const uint32_t tO = tS + 128;
+    const uint32_t tO = tS + C::T_O;
+    const uint32_t tP = tS + C::T_P;
     float m = -INFINITY;
     float l = 0.f;
     bool ok = nkv > 0;
-    uint8_t* prow = sP + slot * C::P_BYTES + r * 128;
-    const int sw = r & 7;
     for (int j = 0; j < nkv; ++j) {
       if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_s_full[slot], j & 1, 8))) {
         ok = false;
@@ -273,19 +274,35 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tc_fence_before();
       mbar_arrive(&bar_s_free[slot]);
 
+      // Row max of the raw scores in 8 independent chains; the causal mask
+      // only exists on the diagonal tile (warp-uniform branch).
       const bool diag = (j == nkv - 1);
-      const int kbase = j * kBN;
-      float mx = -INFINITY;
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        float v = __uint_as_float(sv[c]) * p.scale_log2;
-        if (diag && (kbase + c > qrow)) v = -INFINITY;
-        sv[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      if (diag) {
+        const int lim = qrow - j * kBN;  // keys 0..lim of this tile are visible
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          if (c > lim) sv[c] = __float_as_uint(-INFINITY);
+          mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c]));
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c]));
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-      m = m_new;
+      const float mx2 = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                        p.scale_log2;
+      // Lazy rescaling: the running reference max m (log2 units) only moves
+      // when the tile max exceeds it by more than 8, so P <= 2^8 and O is
+      // rescaled only on those (rare after the first tiles) occasions.
+      float alpha = 1.f;
+      if (mx2 > m + 8.f) {
+        alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mx2);
+        m = mx2;
+      }
+      const float neg_m = -m;
 
       if (j > 0) {
         // PV of the previous tile must be finished before the P tile is
@@ -296,30 +313,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         tc_fence_after();
       }
-      // P = exp2(s - m) rounded to T, streamed into the swizzled K-major tile:
-      // two 64-key halves of [128 rows][128 B]; 16-byte chunk ch of row r
-      // lives at chunk ch ^ (r & 7).
-      float sum = 0.f;
+      // P = exp2(s * scale_log2 - m) rounded to T, packed two per column and
+      // stored to this row's TMEM lane (the A operand of the P V product)
+      float sum8[8];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c0 = half * 64 + ch * 8;
-          float e[8];
+      for (int ch = 0; ch < kBN / 32; ++ch) {
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            e[i] = fast_exp2(__uint_as_float(sv[c0 + i]) - m_new);
-            sum += e[i];
-          }
-          uint4 w;
-          w.x = pack2<T>(e[0], e[1]);
-          w.y = pack2<T>(e[2], e[3]);
-          w.z = pack2<T>(e[4], e[5]);
-          w.w = pack2<T>(e[6], e[7]);
-          *reinterpret_cast<uint4*>(prow + half * (kBM * 128) + ((ch ^ sw) * 16)) = w;
+        for (int i = 0; i < 32; i += 2) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[ch * 32 + i]), p.scale_log2, neg_m));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[ch * 32 + i + 1]), p.scale_log2, neg_m));
+          sum8[i & 7] += e0;
+          sum8[(i + 1) & 7] += e1;
+          pk[i >> 1] = pack2<T>(e0, e1);
         }
+        tmem_st16(tP + ch * 16, pk);
       }
-      l = l * alpha + sum;
+      l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
       if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
@@ -332,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         tmem_st_wait();
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bar_p_full[slot]);
     }

@@ -60,7 +60,7 @@ __device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
 //   ADD: s = round_to<TR>(x + r) is stored as new_residual and normalised.
 // ---------------------------------------------------------------------------
 template <typename TX, typename TW, typename TY, typename TR, bool ADD, int NC>
-__global__ void __launch_bounds__(kWarps * 32) rms_fwd_vec(const TX* __restrict__ x, const TX* __restrict__ r,
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_vec(const TX* __restrict__ x, const TR* __restrict__ r,
                                                            const TW* __restrict__ w, TR* __restrict__ new_res,
                                                            TY* __restrict__ y, float* __restrict__ rstd,
                                                            int64_t rows, int dim, float eps) {
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_vec(const TX* __restrict_
       load8<TX>(xr + col, v[c]);
       if constexpr (ADD) {
         float rv[8];
-        load8<TX>(r + row * dim + col, rv);
+        load8<TR>(r + row * dim + col, rv);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[c][i] = round_to<TR>(v[c][i] + rv[i]);
         store8<TR>(new_res + row * dim + col, v[c]);
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_vec(const TX* __restrict_
 // Generic forward (any dim / alignment): one warp per row, scalar accesses,
 // two passes over the row.
 template <typename TX, typename TW, typename TY, typename TR, bool ADD>
-__global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restrict__ x, const TX* __restrict__ r,
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restrict__ x, const TR* __restrict__ r,
                                                               const TW* __restrict__ w, TR* __restrict__ new_res,
                                                               TY* __restrict__ y, float* __restrict__ rstd,
                                                               int64_t rows, int dim, float eps) {
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restri
   for (int col = lane; col < dim; col += 32) {
     float s = to_f32<TX>(x[row * dim + col]);
     if constexpr (ADD) {
-      s = round_to<TR>(s + to_f32<TX>(r[row * dim + col]));
+      s = round_to<TR>(s + to_f32<TR>(r[row * dim + col]));
       new_res[row * dim + col] = from_f32<TR>(s);
     }
     ss = fmaf(s, s, ss);
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restri
   if (lane == 0) rstd[row] = inv;
   for (int col = lane; col < dim; col += 32) {
     float s = to_f32<TX>(x[row * dim + col]);
-    if constexpr (ADD) s = round_to<TR>(s + to_f32<TX>(r[row * dim + col]));
+    if constexpr (ADD) s = round_to<TR>(s + to_f32<TR>(r[row * dim + col]));
     y[row * dim + col] = from_f32<TY>(s * inv * to_f32<TW>(w[col]));
   }
 }
@@ -279,7 +279,7 @@ int launch_fwd(const void* x, const void* r, const void* w, void* new_res, void*
   const dim3 grid((unsigned)((rows + kWarps - 1) / kWarps));
   const dim3 block(kWarps * 32);
   auto X = static_cast<const TX*>(x);
-  auto R = static_cast<const TX*>(r);
+  auto R = static_cast<const TR*>(r);
   auto W = static_cast<const TW*>(w);
   auto NR = static_cast<TR*>(new_res);
   auto Y = static_cast<TY*>(y);
@@ -434,16 +434,18 @@ int mt_add_rms_norm_fwd(const void* hidden, const void* residual, int act_dtype,
   auto s = static_cast<cudaStream_t>(stream);
   using bf = __nv_bfloat16;
   using hf = __half;
-  if (res_dtype != act_dtype) return MT_ERR_UNSUPPORTED_DTYPE;
-  switch (key3(act_dtype, w_dtype, normed_dtype)) {
-#define CASE(a, b, c, TA, TB, TC)                                                                                  \
-  case key3(a, b, c):                                                                                              \
-    return launch_fwd<true, TA, TB, TC, TA>(hidden, residual, w, new_residual, normed, rstd, rows, dim, eps, s);
-    CASE(MT_BF16, MT_BF16, MT_BF16, bf, bf, bf)
-    CASE(MT_F16, MT_F16, MT_F16, hf, hf, hf)
-    CASE(MT_F32, MT_F32, MT_F32, float, float, float)
-    CASE(MT_BF16, MT_F32, MT_BF16, bf, float, bf)
-    CASE(MT_F32, MT_F32, MT_BF16, float, float, bf)
+  // residual input and new residual share res_dtype; hidden may be narrower
+  // (the model adds a bf16 branch output into its fp32 residual stream)
+  switch (key3(act_dtype, w_dtype, normed_dtype) | (res_dtype << 6)) {
+#define CASE(a, b, c, d, TA, TB, TC, TD)                                                                         \
+  case key3(a, b, c) | (d << 6):                                                                                 \
+    return launch_fwd<true, TA, TB, TC, TD>(hidden, residual, w, new_residual, normed, rstd, rows, dim, eps, s);
+    CASE(MT_BF16, MT_BF16, MT_BF16, MT_BF16, bf, bf, bf, bf)
+    CASE(MT_F16, MT_F16, MT_F16, MT_F16, hf, hf, hf, hf)
+    CASE(MT_F32, MT_F32, MT_F32, MT_F32, float, float, float, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, MT_BF16, bf, float, bf, bf)
+    CASE(MT_F32, MT_F32, MT_BF16, MT_F32, float, float, bf, float)
+    CASE(MT_BF16, MT_F32, MT_BF16, MT_F32, bf, float, bf, float)
 #undef CASE
     default: return MT_ERR_UNSUPPORTED_DTYPE;
   }

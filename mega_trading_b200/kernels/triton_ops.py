@@ -125,18 +125,19 @@ class _AddRMSNorm(torch.autograd.Function):
         w = weight.contiguous()
         dim = x.shape[-1]
         rows = x.numel() // dim if dim else 0
-        new_res = torch.empty_like(x)
+        new_res = torch.empty_like(r)  # residual dtype (may be wider than hidden's)
         normed = torch.empty(x.shape, device=x.device, dtype=out_dtype)
         rstd = torch.empty((rows,), device=x.device, dtype=torch.float32)
         st = lib.mt_add_rms_norm_fwd(
             x.data_ptr(), r.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), _lib.dtype_code(w.dtype),
-            new_res.data_ptr(), _lib.dtype_code(x.dtype), normed.data_ptr(), _lib.dtype_code(out_dtype),
+            new_res.data_ptr(), _lib.dtype_code(r.dtype), normed.data_ptr(), _lib.dtype_code(out_dtype),
             rstd.data_ptr(), rows, dim, float(eps), _dev_stream(x),
         )
         _lib.check(st, "add_rms_norm forward")
         _lib.count(1)
         ctx.save_for_backward(new_res, w, rstd)
-        return new_res.view(hidden.shape), normed.view(hidden.shape)
+        ctx.hidden_dtype = hidden.dtype
+        return new_res.view(residual.shape), normed.view(hidden.shape)
 
     @staticmethod
     def backward(ctx, grad_new_residual, grad_normed):
@@ -146,19 +147,21 @@ class _AddRMSNorm(torch.autograd.Function):
         if grad_normed is None:
             grad_normed = torch.zeros(new_res.shape, device=new_res.device, dtype=new_res.dtype)
         dx, dw = _rms_bwd(new_res, w, rstd, grad_normed.contiguous(), new_res.dtype,
-                          residual_grad=grad_new_residual.contiguous())
+                          residual_grad=grad_new_residual.to(new_res.dtype).contiguous())
         # both add inputs receive the same gradient (triton_ops.py:288-291)
-        return dx, dx, dw, None, None
+        dh = dx if ctx.hidden_dtype == dx.dtype else dx.to(ctx.hidden_dtype)
+        return dh, dx, dw, None, None
 
 
 def add_rms_norm(hidden, residual, weight, *, eps: float, out_dtype: torch.dtype | None = None):
-    """Fused ``new_residual = hidden + residual`` and ``RMSNorm(new_residual)``."""
+    """Fused ``new_residual = hidden + residual`` and ``RMSNorm(new_residual)``.
+
+    ``residual`` may be wider than ``hidden`` (fp32 residual stream, bf16 branch
+    output); ``new_residual`` takes the residual's dtype."""
     _require(hidden, "add_rms_norm")
     _require(residual, "add_rms_norm")
     if hidden.shape != residual.shape:
         raise ValueError("hidden and residual must have the same shape")
-    if hidden.dtype != residual.dtype:
-        raise ValueError("hidden and residual must have the same dtype")
     if hidden.shape[-1] != weight.numel():
         raise ValueError("weight must have one entry per hidden feature")
     return _AddRMSNorm.apply(hidden, residual, weight, float(eps), out_dtype or hidden.dtype)
@@ -167,6 +170,9 @@ def add_rms_norm(hidden, residual, weight, *, eps: float, out_dtype: torch.dtype
 def triton_add_rms_norm(hidden: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, *,
                         eps: float) -> tuple[torch.Tensor, torch.Tensor]:
     """Fused residual-add + RMSNorm; returns ``(new_residual, normed)``."""
+    _require(hidden, "triton_add_rms_norm")
+    if hidden.dtype != residual.dtype:
+        raise ValueError("hidden and residual must have the same dtype")
     return add_rms_norm(hidden, residual, weight, eps=eps)
 
 

@@ -135,6 +135,15 @@ class LlamaDecoderBlock(nn.Module):
         h = h + self.attention(self.attention_norm(h))
         return h + self.feed_forward(self.ffn_norm(h))
 
+    def forward_fused(self, h: torch.Tensor, x: torch.Tensor, next_norm: "RMSNorm") -> tuple[torch.Tensor, torch.Tensor]:
+        """Same block with each residual add fused into the following RMSNorm.
+
+        ``x`` is ``attention_norm(h)`` (already computed by the previous fused
+        add); returns ``(h_out, next_norm(h_out))``."""
+        h, x = _ops.add_rms_norm(self.attention(x), h, self.ffn_norm.weight, eps=self.ffn_norm.eps,
+                                 out_dtype=_BF16)
+        return _ops.add_rms_norm(self.feed_forward(x), h, next_norm.weight, eps=next_norm.eps, out_dtype=_BF16)
+
 
 class TradingModelB200(nn.Module):
     """The reference ``TradingModel`` (dropout 0) on the sm_100a operators."""
@@ -155,9 +164,14 @@ class TradingModelB200(nn.Module):
         if input_ids.shape[1] > self.cfg.block_size:
             raise ValueError(f"sequence length {input_ids.shape[1]} exceeds block_size {self.cfg.block_size}")
         h = self.token_embedding(input_ids)  # fp32 residual stream
-        for block in self.blocks:
-            h = block(h)
-        return self.norm(h)
+        if not self.blocks:
+            return self.norm(h)
+        # every residual add runs fused with the RMSNorm that follows it
+        x = self.blocks[0].attention_norm(h)
+        for i, block in enumerate(self.blocks):
+            nxt = self.blocks[i + 1].attention_norm if i + 1 < len(self.blocks) else self.norm
+            h, x = block.forward_fused(h, x, nxt)
+        return x
 
     def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
         """Mean next-token loss when ``labels`` is given (the training entry), else logits."""
