@@ -48,7 +48,7 @@ namespace {
 
 constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
-constexpr int kNQ = 2;    // Q/dO pipeline stages
+constexpr int kNQ = 3;    // Q/dO pipeline stages (loads run ~2 tiles ahead of the MMAs)
 constexpr int kThreads = 320;
 constexpr uint32_t kKernelId = 2;
 
@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
   uint64_t* bar_dq_full = bar_sd_full + 3;
   uint64_t* bar_dq_free = bar_sd_full + 4;
   uint64_t* bar_done = bar_sd_full + 5;
+  uint64_t* bar_pt_free = bar_sd_full + 6;  // dV of the previous tile done: P^T TMEM free
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
     mbar_init(bar_dq_full, 1);
     mbar_init(bar_dq_free, 256);
     mbar_init(bar_done, 1);
+    mbar_init(bar_pt_free, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -276,9 +278,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),
                   idesc_acc, acc);
+        }
+        umma_commit(bar_pt_free);
+#pragma unroll
+        for (int kk = 0; kk < kBQ / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          const uint32_t b_off = kk * 16 * C::ROW_BYTES;
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
                   make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
         }
+        umma_commit(&bar_q_empty[st]);  // Q/dO of this stage are no longer read (dQ reads K and dS)
         if (it > 0 && !wait_bounded(wc, bar_dq_free, (it - 1) & 1, 6)) {
           ok = false;
           break;
@@ -292,7 +302,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
                   kk > 0 ? 1u : 0u);
         }
         umma_commit(bar_dq_full);
-        umma_commit(&bar_q_empty[st]);
       }
       // every issued MMA completes before TMEM is released (also on abort)
       umma_commit(bar_done);
@@ -315,20 +324,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       // the previous reduce of this warpgroup must have finished reading staging
       if (leader) bulk_wait_group_read0();
       named_bar_sync(1 + wg, 128);
-      // 16 columns at a time: TMEM -> registers -> fp32 staging (box bx = 32
-      // columns x 128 rows, 128 B rows, 128B swizzle)
+      // TMEM -> registers -> fp32 staging (box bx = 32 columns x 128 rows,
+      // 128 B rows, 128B swizzle)
+      if constexpr (kCols == 32) {
+        uint32_t qa[16], qb[16];
+        tmem_ld16(tmem + lane_off + C::T_DQ + wg * 32, qa);
+        tmem_ld16(tmem + lane_off + C::T_DQ + wg * 32 + 16, qb);
+        tmem_ld_wait_regs(qa, qb);
 #pragma unroll
-      for (int half = 0; half < kCols / 16; ++half) {
-        uint32_t qv[16];
-        tmem_ld16(tmem + lane_off + C::T_DQ + wg * kCols + half * 16, qv);
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t* src = q < 4 ? &qa[q * 4] : &qb[(q - 4) * 4];
+          const int col = wg * 32 + q * 4;
+          const int ch = (col & 31) >> 2;
+          *reinterpret_cast<uint4*>(sDQ + (col >> 5) * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16)) =
+              make_uint4(src[0], src[1], src[2], src[3]);
+        }
+      } else {
+        uint32_t qa[16], qb[16];
+        tmem_ld16(tmem + lane_off + C::T_DQ + wg * 16, qa);
         tmem_ld_wait();
 #pragma unroll
+        for (int i = 0; i < 16; ++i) qb[i] = 0u;
+        tmem_ld_wait_regs(qa, qb);
+#pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int col = wg * kCols + half * 16 + q * 4;
-          const int bx = col >> 5;
+          const int col = wg * 16 + q * 4;
           const int ch = (col & 31) >> 2;
-          *reinterpret_cast<uint4*>(sDQ + bx * (128 * 128) + r * 128 + ((ch ^ (r & 7)) * 16)) =
-              make_uint4(qv[q * 4], qv[q * 4 + 1], qv[q * 4 + 2], qv[q * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDQ + r * 128 + ((ch ^ (r & 7)) * 16)) =
+              make_uint4(qa[q * 4], qa[q * 4 + 1], qa[q * 4 + 2], qa[q * 4 + 3]);
         }
       }
       tc_fence_before();
@@ -369,29 +392,67 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       const float* dl = sDelta + st * 128;
       // P^T and dS^T rows for this warpgroup's 64 query columns, packed in
       // registers until the previous tile's products have released the tiles
-      uint32_t pk[2][16], dk[2][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      uint32_t pk0[16], pk1[16], dk[2][16];
+      // S^T / dP^T columns of this warpgroup in four 16-column chunks; the
+      // TMEM loads of chunk c+1 are in flight while chunk c is processed.
+      auto process = [&](int c, const uint32_t (&sv)[16], const uint32_t (&dv)[16]) {
         const int col0 = wg * 64 + c * 16;
-        uint32_t sv[16], dv[16];
-        tmem_ld16(tmem + lane_off + C::T_S + col0, sv);
-        tmem_ld16(tmem + lane_off + C::T_DP + col0, dv);
-        tmem_ld_wait();
         const int lim = key - (qi * kBQ + col0);  // column i is masked when i < lim (key > query)
+        float lv[16], dlv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(lse + col0 + i);
+          const float4 d = *reinterpret_cast<const float4*>(dl + col0 + i);
+          lv[i] = a.x; lv[i + 1] = a.y; lv[i + 2] = a.z; lv[i + 3] = a.w;
+          dlv[i] = d.x; dlv[i + 1] = d.y; dlv[i + 2] = d.z; dlv[i + 3] = d.w;
+        }
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse[col0 + i]));
-          float p1 = fast_exp2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -lse[col0 + i + 1]));
+          float p0 = fast_exp2(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lv[i]));
+          float p1 = fast_exp2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -lv[i + 1]));
           if (diag) {
             if (i < lim) p0 = 0.f;
             if (i + 1 < lim) p1 = 0.f;
           }
-          const float d0 = p0 * (__uint_as_float(dv[i]) - dl[col0 + i]);
-          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dl[col0 + i + 1]);
-          pk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
+          const float d0 = p0 * (__uint_as_float(dv[i]) - dlv[i]);
+          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dlv[i + 1]);
+          if (c < 2)
+            pk0[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
+          else
+            pk1[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
           dk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(d0, d1);
         }
+      };
+      {
+        const uint32_t ts = tmem + lane_off + C::T_S + wg * 64;
+        const uint32_t td = tmem + lane_off + C::T_DP + wg * 64;
+        uint32_t sa[16], da[16], sb[16], db[16];
+        tmem_ld16(ts, sa);
+        tmem_ld16(td, da);
+        tmem_ld_wait_regs(sa, da);
+        tmem_ld16(ts + 16, sb);
+        tmem_ld16(td + 16, db);
+        process(0, sa, da);
+        tmem_ld_wait_regs(sb, db);
+        tmem_ld16(ts + 32, sa);
+        tmem_ld16(td + 32, da);
+        process(1, sb, db);
+        // P^T -> TMEM as soon as dV of the previous tile has released it
+        if (it > 0 && !bar_all(wait_bounded(wc, bar_pt_free, (it - 1) & 1, 7), 4, 256)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          tmem_st16(tmem + lane_off + C::T_PT + wg * 32, pk0);
+        }
+        tmem_ld_wait_regs(sa, da);
+        tmem_ld16(ts + 48, sb);
+        tmem_ld16(td + 48, db);
+        process(2, sa, da);
+        tmem_ld_wait_regs(sb, db);
+        process(3, sb, db);
+        if (ok) tmem_st16(tmem + lane_off + C::T_PT + wg * 32 + 16, pk1);
       }
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive(bar_sd_free);
       // dV/dK/dQ of the previous tile are complete once its dQ is: then the
@@ -400,9 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
         ok = false;
         break;
       }
-      // P^T rows -> TMEM (this warpgroup's 64 query columns = 32 packed columns)
-      tmem_st16(tmem + lane_off + C::T_PT + wg * 32, pk[0]);
-      tmem_st16(tmem + lane_off + C::T_PT + wg * 32 + 16, pk[1]);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int col0 = wg * 64 + c * 32;
