@@ -157,6 +157,15 @@ MT_API int mt_swiglu_fwd(const void* g, const void* u, void* y, int dtype, int64
 MT_API int mt_swiglu_bwd(const void* g, const void* u, const void* dy, void* dg,
                   void* du, int dtype, int64_t n, void* stream);
 
+/* Packed variant for a single GEMM against concatenated [w1; w3] weights:
+ * gu is [rows, 2*inter] = [gate | up] per row, y is [rows, inter]; the
+ * backward writes the packed gradient dgu [rows, 2*inter].  bf16/fp16,
+ * inter % 8 == 0.  Same math as mt_swiglu_fwd / mt_swiglu_bwd. */
+MT_API int mt_swiglu_packed_fwd(const void* gu, void* y, int dtype, int64_t rows,
+                                int64_t inter, void* stream);
+MT_API int mt_swiglu_packed_bwd(const void* gu, const void* dy, void* dgu, int dtype,
+                                int64_t rows, int64_t inter, void* stream);
+
 /* ---------------------------------------------------------------------
  * Causal GQA flash attention (tcgen05 + TMEM + TMA)   replaces triton_attention
  *   (src/mega_trading/kernels/triton_attention.py:12-24, forward :27-78 and

@@ -56,6 +56,8 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     ),
     "mt_swiglu_fwd": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_vp]),
     "mt_swiglu_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp]),
+    "mt_swiglu_packed_fwd": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "mt_swiglu_packed_bwd": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
     "mt_attention_fwd": (
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p, c_i64p,

@@ -183,6 +183,49 @@ __global__ void __launch_bounds__(kThreads) swiglu_bwd_k(const T* __restrict__ g
   }
 }
 
+
+// Packed SwiGLU: gu = [gate | up] rows of width 2 * inter (one GEMM with the
+// concatenated w1 / w3 weights), y = silu(gate) * up of width inter; the
+// backward writes the packed gradient [dgate | dup] for one backward GEMM.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) swiglu_packed_fwd_k(const T* __restrict__ gu, T* __restrict__ y,
+                                                                 uint32_t total, FastDiv vpr, int inter) {
+  constexpr int V = 16 / sizeof(T);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int64_t r = vpr.div(i);
+    const int c = int(i - uint32_t(r) * vpr.d) * V;
+    float gv[V], uv[V], o[V];
+    load_vec<T, V>(gu + r * 2 * inter + c, gv);
+    load_vec<T, V>(gu + r * 2 * inter + inter + c, uv);
+#pragma unroll
+    for (int j = 0; j < V; ++j) o[j] = round_to<T>(gv[j] * sigmoidf_(gv[j])) * uv[j];
+    store_vec<T, V>(y + r * inter + c, o);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) swiglu_packed_bwd_k(const T* __restrict__ gu, const T* __restrict__ dy,
+                                                                 T* __restrict__ dgu, uint32_t total, FastDiv vpr,
+                                                                 int inter) {
+  constexpr int V = 16 / sizeof(T);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int64_t r = vpr.div(i);
+    const int c = int(i - uint32_t(r) * vpr.d) * V;
+    float gv[V], uv[V], dv[V], og[V], ou[V];
+    load_vec<T, V>(gu + r * 2 * inter + c, gv);
+    load_vec<T, V>(gu + r * 2 * inter + inter + c, uv);
+    load_vec<T, V>(dy + r * inter + c, dv);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float s = sigmoidf_(gv[j]);
+      og[j] = dv[j] * uv[j] * s * (1.f + gv[j] * (1.f - s));
+      ou[j] = dv[j] * round_to<T>(gv[j] * s);
+    }
+    store_vec<T, V>(dgu + r * 2 * inter + c, og);
+    store_vec<T, V>(dgu + r * 2 * inter + inter + c, ou);
+  }
+}
+
 }  // namespace
 }  // namespace mt
 
@@ -280,6 +323,47 @@ int mt_swiglu_bwd(const void* g, const void* u, const void* dy, void* dg, void* 
                                                           static_cast<const TT*>(dy), static_cast<TT*>(dg),
                                                           static_cast<TT*>(du), n);
     return check_launch("swiglu_bwd");
+  });
+}
+
+
+int mt_swiglu_packed_fwd(const void* gu, void* y, int dtype, int64_t rows, int64_t inter, void* stream) {
+  if (rows < 0 || inter <= 0) return MT_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return MT_OK;
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (inter % 8 != 0 || !aligned16(gu) || !aligned16(y)) return MT_ERR_UNSUPPORTED_LAYOUT;
+  if (rows * inter / 8 >= (int64_t(1) << 31)) return MT_ERR_INVALID_ARGUMENT;
+  auto s = static_cast<cudaStream_t>(stream);
+  return with_half_dtype(dtype, [&](auto tv) {
+    using TT = decltype(tv);
+    if constexpr (sizeof(TT) == 2) {
+      FastDiv vpr;
+      vpr.init((uint32_t)(inter / 8));
+      swiglu_packed_fwd_k<TT><<<grid_for(rows * inter / 8), kThreads, 0, s>>>(
+          static_cast<const TT*>(gu), static_cast<TT*>(y), (uint32_t)(rows * inter / 8), vpr, (int)inter);
+    }
+    return check_launch("swiglu_packed_fwd");
+  });
+}
+
+int mt_swiglu_packed_bwd(const void* gu, const void* dy, void* dgu, int dtype, int64_t rows, int64_t inter,
+                         void* stream) {
+  if (rows < 0 || inter <= 0) return MT_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return MT_OK;
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (inter % 8 != 0 || !aligned16(gu) || !aligned16(dy) || !aligned16(dgu)) return MT_ERR_UNSUPPORTED_LAYOUT;
+  if (rows * inter / 8 >= (int64_t(1) << 31)) return MT_ERR_INVALID_ARGUMENT;
+  auto s = static_cast<cudaStream_t>(stream);
+  return with_half_dtype(dtype, [&](auto tv) {
+    using TT = decltype(tv);
+    if constexpr (sizeof(TT) == 2) {
+      FastDiv vpr;
+      vpr.init((uint32_t)(inter / 8));
+      swiglu_packed_bwd_k<TT><<<grid_for(rows * inter / 8), kThreads, 0, s>>>(
+          static_cast<const TT*>(gu), static_cast<const TT*>(dy), static_cast<TT*>(dgu), (uint32_t)(rows * inter / 8),
+          vpr, (int)inter);
+    }
+    return check_launch("swiglu_packed_bwd");
   });
 }
 

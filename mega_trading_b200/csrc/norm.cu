@@ -21,7 +21,7 @@ namespace {
 
 constexpr int kWarps = 8;           // rows in flight per block
 constexpr int kChunk = 8;           // elements per lane per chunk
-constexpr int kBwdBlocksPerSM = 2;  // persistent backward grid
+constexpr int kBwdBlocksPerSM = 3;  // persistent backward grid (3 resident blocks per SM)
 
 // Load / store 8 consecutive elements as floats (16 or 32 bytes).
 template <typename T>
@@ -136,39 +136,38 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restri
 //   dn   = dy * w
 //   dx   = rstd * (dn - x * rstd^2 * sum(dn * x) / dim)  (+ g_res if GRES)
 //   dw_p = sum_rows dy * x * rstd                       (per block partial)
+// Only the dW partials live in registers across rows; each row is read twice
+// (dot product, then dx), the second time from L1, so three blocks of eight
+// warps fit per SM and enough rows are in flight to stream at HBM speed.
 // ---------------------------------------------------------------------------
 template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES, int NC>
-__global__ void __launch_bounds__(kWarps * 32) rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w,
-                                                           const float* __restrict__ rstd, const TG* __restrict__ dy,
-                                                           const TGR* __restrict__ gres, TD* __restrict__ dx,
-                                                           float* __restrict__ partial, int64_t rows, int dim) {
+__global__ void __launch_bounds__(kWarps * 32, (NC <= 4 ? 3 : 1))
+    rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rstd,
+                const TG* __restrict__ dy, const TGR* __restrict__ gres, TD* __restrict__ dx,
+                float* __restrict__ partial, int64_t rows, int dim) {
   extern __shared__ float red[];  // [kWarps][dim]
   const int lane = lane_id();
   const int warp = warp_id();
-  float wv[NC][8];
   float acc[NC][8];
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int col = (c * 32 + lane) * kChunk;
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
-    if (col < dim) load8<TW>(w + col, wv[c]);
-  }
   for (int64_t row = int64_t(blockIdx.x) * kWarps + warp; row < rows; row += int64_t(gridDim.x) * kWarps) {
     const float inv = rstd[row];
-    float xv[NC][8], gv[NC][8];
+    const TX* xr = x + row * dim;
+    const TG* gr_ = dy + row * dim;
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int col = (c * 32 + lane) * kChunk;
       if (col < dim) {
-        load8<TX>(x + row * dim + col, xv[c]);
-        load8<TG>(dy + row * dim + col, gv[c]);
+        float xv[8], gv[8], wv[8];
+        load8<TX>(xr + col, xv);
+        load8<TG>(gr_ + col, gv);
+        load8<TW>(w + col, wv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          dot = fmaf(gv[c][i] * wv[c][i], xv[c][i], dot);
-          acc[c][i] = fmaf(gv[c][i], xv[c][i] * inv, acc[c][i]);
-        }
+        for (int i = 0; i < 8; ++i) dot = fmaf(gv[i] * wv[i], xv[i], dot);
       }
     }
     dot = warp_sum(dot);
@@ -177,13 +176,17 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_vec(const TX* __restrict_
     for (int c = 0; c < NC; ++c) {
       const int col = (c * 32 + lane) * kChunk;
       if (col < dim) {
-        float o[8];
-        float gr[8];
-        if constexpr (GRES) load8<TGR>(gres + row * dim + col, gr);
+        float xv[8], gv[8], wv[8], o[8];
+        load8<TX>(xr + col, xv);
+        load8<TG>(gr_ + col, gv);
+        load8<TW>(w + col, wv);
+        float rg[8];
+        if constexpr (GRES) load8<TGR>(gres + row * dim + col, rg);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          o[i] = inv * (gv[c][i] * wv[c][i] - xv[c][i] * k);
-          if constexpr (GRES) o[i] += gr[i];
+          o[i] = inv * (gv[i] * wv[i] - xv[i] * k);
+          if constexpr (GRES) o[i] += rg[i];
+          acc[c][i] = fmaf(gv[i], xv[i] * inv, acc[c][i]);
         }
         store8<TD>(dx + row * dim + col, o);
       }
@@ -237,13 +240,24 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_scalar(const TX* __restri
   }
 }
 
+// Second stage: dw[col] = sum over blocks of partial[block][col], in a fixed
+// order (32 row-lanes per column, then a tree over the lanes).
 template <typename TW>
-__global__ void dw_reduce(const float* __restrict__ partial, int nblocks, int dim, TW* __restrict__ dw) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= dim) return;
-  float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partial[int64_t(b) * dim + col];
-  dw[col] = from_f32<TW>(s);
+__global__ void __launch_bounds__(1024) dw_reduce(const float* __restrict__ partial, int nblocks, int dim,
+                                                  TW* __restrict__ dw) {
+  __shared__ float s[32][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  float v = 0.f;
+  if (col < dim)
+    for (int b = threadIdx.y; b < nblocks; b += 32) v += partial[int64_t(b) * dim + col];
+  s[threadIdx.y][threadIdx.x] = v;
+  __syncthreads();
+  if (threadIdx.y == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t += s[i][threadIdx.x];
+    if (col < dim) dw[col] = from_f32<TW>(t);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -263,9 +277,8 @@ int with_dtype(int code, F&& f) {
 
 int chunks_for(int64_t dim) {
   const int64_t per_lane = (dim + 32 * kChunk - 1) / (32 * kChunk);
-  if (per_lane <= 1) return 1;
-  if (per_lane <= 2) return 2;
-  if (per_lane <= 4) return 4;
+  if (per_lane <= 4) return (int)per_lane;  // 1, 2, 3, 4
+  if (per_lane <= 6) return 6;
   if (per_lane <= 8) return 8;
   return 0;  // too wide for the register-resident path
 }
@@ -288,7 +301,9 @@ int launch_fwd(const void* x, const void* r, const void* w, void* new_res, void*
     switch (nc) {
       case 1: rms_fwd_vec<TX, TW, TY, TR, ADD, 1><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
       case 2: rms_fwd_vec<TX, TW, TY, TR, ADD, 2><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+      case 3: rms_fwd_vec<TX, TW, TY, TR, ADD, 3><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
       case 4: rms_fwd_vec<TX, TW, TY, TR, ADD, 4><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
+      case 6: rms_fwd_vec<TX, TW, TY, TR, ADD, 6><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
       default: rms_fwd_vec<TX, TW, TY, TR, ADD, 8><<<grid, block, 0, stream>>>(X, R, W, NR, Y, rstd, rows, d, eps); break;
     }
   } else {
@@ -327,7 +342,9 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     switch (nc) {
       case 1: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1>; break;
       case 2: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2>; break;
+      case 3: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3>; break;
       case 4: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4>; break;
+      case 6: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6>; break;
       default: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8>; break;
     }
     int st = set_smem_limit(fn, smem);
@@ -335,7 +352,9 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     switch (nc) {
       case 1: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
       case 2: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      case 3: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
       case 4: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      case 6: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
       default: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
     }
   } else {
@@ -343,7 +362,7 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
   }
   int st = check_launch(GRES ? "add_rms_norm_bwd" : "rms_norm_bwd");
   if (st != MT_OK) return st;
-  dw_reduce<TDW><<<(d + 255) / 256, 256, 0, stream>>>(partial, nblocks, d, static_cast<TDW*>(dw));
+  dw_reduce<TDW><<<(d + 31) / 32, dim3(32, 32), 0, stream>>>(partial, nblocks, d, static_cast<TDW*>(dw));
   return check_launch("rms_norm_dw_reduce");
 }
 

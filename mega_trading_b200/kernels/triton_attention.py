@@ -40,13 +40,13 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     return o, lse
 
 
-def _launch_bwd(q, k, v, o, lse, do, scale: float):
+def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None):
     lib = _lib.load()
     B, Hq, T, D = q.shape
     Hkv = k.shape[1]
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
     ws_bytes = int(lib.mt_attention_bwd_workspace_bytes(B, Hq, T, D))
     ws = torch.empty((max(ws_bytes, 16),), device=q.device, dtype=torch.uint8)
     status = _lib.status_word(q.device)

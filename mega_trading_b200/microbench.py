@@ -175,6 +175,18 @@ def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65
             mf, mb = _time(f, iters), _time(b, iters)
             out.append({"op": "swiglu", "N": n, "I": I, "fwd_ms": mf, "fwd_gbs": 3 * n * I * 2 / mf / 1e6,
                         "bwd_ms": mb, "bwd_gbs": 5 * n * I * 2 / mb / 1e6})
+        gu = torch.cat([gt, up], dim=1)
+        dgu = torch.empty_like(gu)
+        f = lambda: lib.mt_swiglu_packed_fwd(gu.data_ptr(), y.data_ptr(), 2, n, I, st)  # noqa: E731
+        b = lambda: lib.mt_swiglu_packed_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), 2, n, I, st)  # noqa: E731
+        if profile:
+            for _ in range(iters):
+                f()
+                b()
+        else:
+            mf, mb = _time(f, iters), _time(b, iters)
+            out.append({"op": "swiglu_packed", "N": n, "I": I, "fwd_ms": mf, "fwd_gbs": 3 * n * I * 2 / mf / 1e6,
+                        "bwd_ms": mb, "bwd_gbs": 5 * n * I * 2 / mb / 1e6})
     return out
 
 

@@ -23,6 +23,7 @@ from torch import nn
 
 from .kernels import triton_attention as _attn
 from .kernels import triton_ops as _ops
+from .kernels.fused_blocks import qkv_rope_attention, swiglu_packed
 from .kernels.fused_ce import fused_linear_cross_entropy
 
 
@@ -101,12 +102,22 @@ class LlamaAttention(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, H = x.shape
+        # one projection GEMM against [q_proj; k_proj; v_proj]; RoPE + attention
+        # read the packed output in place and write one packed gradient
+        w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], dim=0).to(_BF16)
+        qkv = F.linear(x, w_qkv)
+        o = qkv_rope_attention(qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
+        # o is stored [B, T, H, D]: the transpose is free
+        return F.linear(o.transpose(1, 2).reshape(B, T, H), _w(self.o_proj.weight))
+
+    def forward_unfused(self, x: torch.Tensor) -> torch.Tensor:
+        """Operator-by-operator path through the reference API mirror (same math)."""
+        B, T, H = x.shape
         q = F.linear(x, _w(self.q_proj.weight)).view(B, T, self.heads, self.head_dim).transpose(1, 2)
         k = F.linear(x, _w(self.k_proj.weight)).view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
         v = F.linear(x, _w(self.v_proj.weight)).view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
         q, k = _ops.triton_apply_rope(q, k, self.cos[:T], self.sin[:T])
         o = _attn.triton_attention(q, k, v, repeats=self.repeats)
-        # o keeps q's [B, T, H, D] physical layout: the transpose is free
         return F.linear(o.transpose(1, 2).reshape(B, T, H), _w(self.o_proj.weight))
 
 
@@ -118,6 +129,11 @@ class SwiGLU(nn.Module):
         self.w3 = nn.Linear(cfg.hidden_dim, cfg.intermediate_dim, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        # one GEMM against [w1; w3]; the gate reads [gate | up] in place
+        gu = F.linear(x, torch.cat([self.w1.weight, self.w3.weight], dim=0).to(_BF16))
+        return F.linear(swiglu_packed(gu), _w(self.w2.weight))
+
+    def forward_unfused(self, x: torch.Tensor) -> torch.Tensor:
         gate = F.linear(x, _w(self.w1.weight))
         up = F.linear(x, _w(self.w3.weight))
         return F.linear(_ops.triton_swiglu_gate(gate, up), _w(self.w2.weight))
