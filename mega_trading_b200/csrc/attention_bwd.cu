@@ -84,6 +84,8 @@ struct BwdParams {
   void* dv;
   int64_t dks[4], dvs[4];
   int T, Tp, Hq, Hkv, repeats, n_tiles;
+  int n_heads;  // B * Hkv
+  int group;    // (batch, kv head) pairs whose key tiles are interleaved in launch order
   float scale_log2, scale;
   uint32_t* status;
 };
@@ -152,10 +154,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
-  const int bk = blockIdx.x;
+  // Launch order: groups of `group` (batch, kv head) pairs; inside a group the
+  // key tiles go heaviest (smallest index) first, cycling over the group's
+  // heads.  The CTAs resident at one time then share a few heads' Q / dO
+  // tiles and fp32 dQ rows in L2 instead of streaming every head's.
+  const int per_group = p.group * p.n_tiles;
+  const int grp = (int)blockIdx.x / per_group;
+  const int rem = (int)blockIdx.x - grp * per_group;
+  const int g0 = grp * p.group;
+  const int gsz = min(p.group, p.n_heads - g0);
+  const int kt = rem / gsz;
+  const int bk = g0 + (rem - kt * gsz);
   const int b = bk / p.Hkv;
   const int hk = bk - b * p.Hkv;
-  const int kt = (int)blockIdx.y;  // heaviest (smallest) key tiles launch first
   const int n_q = p.n_tiles - kt;  // causal query tiles per head: kt .. n_tiles-1
   const int n_it = n_q * p.repeats;
 
@@ -624,8 +635,14 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
     auto kern = attn_bwd_kernel<T, D>;
     int st = set_smem_limit((const void*)kern, C::SMEM);
     if (st != MT_OK) return st;
-    dim3 grid((unsigned)(B * prm.Hkv), (unsigned)prm.n_tiles);
-    kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
+    // group size: about 32 MB of Q + dO (16-bit) and fp32 dQ rows per group
+    const int64_t head_bytes = int64_t(prm.repeats) * prm.Tp * D * 8;
+    const int64_t g = (int64_t(32) << 20) / (head_bytes > 0 ? head_bytes : 1);
+    prm.n_heads = B * prm.Hkv;
+    prm.group = (int)(g < 1 ? 1 : (g > prm.n_heads ? prm.n_heads : g));
+    const int64_t blocks = int64_t(prm.n_heads) * prm.n_tiles;
+    if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+    kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
     st = check_launch("attention_bwd");
     if (st != MT_OK) return st;
   }

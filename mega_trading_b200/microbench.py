@@ -2,7 +2,8 @@
 
 ``python -m mega_trading_b200.microbench [--ops attention,ce,rmsnorm,rope,swiglu] [--iters N]``
 
-* attention: config 1 -- B=16, Hq=16, Hkv=4, D=64, T in {1024, 2048, 4096},
+* attention: config 1 -- B=16, Hq=16, Hkv=4, D=64, T in {1024, 2048, 4096}
+  (``--batch 32 --heads 12 --kv-heads 4 --seqs 2048`` is one config-3 layer),
   q/k/v ~ N(0,1)*0.5, dO ~ N(0,1), forward and backward, TFLOP/s with the
   reference's causal FLOP count (``scripts/benchmark_triton_attention.py:179-190``:
   4*B*Hq*D*T(T+1)/2 forward; backward 2.5x forward).
@@ -54,10 +55,10 @@ def _time(fn, iters: int, warm: int = 3) -> float:
     return s.elapsed_time(e) / iters
 
 
-def attention_cases(dev, iters, profile, seqs=(1024, 2048, 4096), batch=16):
+def attention_cases(dev, iters, profile, seqs=(1024, 2048, 4096), batch=16, heads=16, kv_heads=4):
     out = []
     for T in seqs:
-        B, Hq, Hkv, D = batch, 16, 4, 64
+        B, Hq, Hkv, D = batch, heads, kv_heads, 64
         g = torch.Generator(device=dev).manual_seed(T)
         q = (torch.randn(B, Hq, T, D, device=dev, generator=g) * 0.5).bfloat16()
         k = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16()
@@ -75,7 +76,7 @@ def attention_cases(dev, iters, profile, seqs=(1024, 2048, 4096), batch=16):
         flops = 4.0 * B * Hq * D * T * (T + 1) / 2
         ms_f = _time(fwd, iters)
         ms_b = _time(bwd, iters)
-        out.append({"op": "attention", "T": T, "B": B, "fwd_ms": ms_f, "fwd_tflops": flops / ms_f / 1e9,
+        out.append({"op": "attention", "T": T, "B": B, "Hq": Hq, "Hkv": Hkv, "fwd_ms": ms_f, "fwd_tflops": flops / ms_f / 1e9,
                     "bwd_ms": ms_b, "bwd_tflops": 2.5 * flops / ms_b / 1e9,
                     "fwd_bwd_tflops": 3.5 * flops / (ms_f + ms_b) / 1e9})
     return out
@@ -191,12 +192,12 @@ def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65
 
 
 def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0, attn_seqs=(1024, 2048, 4096),
-        attn_batch: int = 16, ce_rows: int = 65536) -> list[dict]:
+        attn_batch: int = 16, ce_rows: int = 65536, heads: int = 16, kv_heads: int = 4) -> list[dict]:
     dev = torch.device("cuda", device)
     torch.cuda.set_device(dev)
     res: list[dict] = []
     if "attention" in ops:
-        res += attention_cases(dev, iters, profile, attn_seqs, attn_batch)
+        res += attention_cases(dev, iters, profile, attn_seqs, attn_batch, heads, kv_heads)
     if "ce" in ops:
         res += ce_cases(dev, iters, profile, n=ce_rows)
     bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
@@ -224,9 +225,11 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--seqs", default="1024,2048,4096")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--ce-rows", type=int, default=65536)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--kv-heads", type=int, default=4)
     args = ap.parse_args(argv)
     res = run(args.ops.split(","), args.iters, args.profile, attn_seqs=tuple(int(s) for s in args.seqs.split(",")),
-              attn_batch=args.batch, ce_rows=args.ce_rows)
+              attn_batch=args.batch, ce_rows=args.ce_rows, heads=args.heads, kv_heads=args.kv_heads)
     for r in res:
         print(json.dumps(r))
     return 0
