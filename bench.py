@@ -32,8 +32,12 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "train tokens/s (config 3: 12L d768 GQA 12/4, seq 2048, global batch 256)"
 GLOBAL_BATCH = 256
 SEQ = 2048
-MICRO_BATCH = 32
+MICRO_BATCH = 128
 CPU_SAMPLE_SEQS = 1
+# DRAM bytes (read + write) of one attn_bwd_kernel launch measured by ncu at
+# B=32, Hq=12, Hkv=4, T=2048, D=64 (profiles/attention_bwd_config3_layer.txt);
+# traffic grows with the batch, so a launch of B sequences moves B/32 times this.
+ATTN_BWD_DRAM_BYTES = (476_131_328 + 225_660_416, 32)
 
 
 def _peaks() -> dict:
@@ -253,6 +257,10 @@ def main(argv: list[str] | None = None) -> int:
     n_bwd, ms_bwd = kern.get("attention_bwd", (0, float("nan")))
     n_fwd, ms_fwd = kern.get("attention_fwd", (0, float("nan")))
     achieved = bwd_flops / (ms_bwd / 1000.0) / 1e12
+    # minimum: q, dO, k, v, lse, delta read once; dq, dk, dv written once (16-bit)
+    rows_q = B * cfg.attention_heads * SEQ
+    rows_kv = B * cfg.kv_heads * SEQ
+    attn_bwd_bytes = (3 * rows_q + 4 * rows_kv) * cfg.head_dim * 2 + rows_q * 8
     kernels = {name: {"launches": n, "mean_ms": ms} for name, (n, ms) in kern.items()}
     if "attention_fwd" in kern:
         kernels["attention_fwd"]["tflops"] = fwd_flops / (ms_fwd / 1000.0) / 1e12
@@ -289,14 +297,19 @@ def main(argv: list[str] | None = None) -> int:
                 "global_batch": GLOBAL_BATCH, "seq_len": SEQ, "micro_batch": micro,
                 "grad_accum": math.ceil(local_batch / micro), "parallelism": f"dp{world}",
                 "optimizer": "fused AdamW, fp32 master weights",
-                "l2": "no flush: per-step working set (activations ~20 GB per micro-batch) is far larger than L2",
+                "l2": f"no flush: per-step working set (activations of {micro} x {SEQ} tokens, tens of GB) "
+                      "is far larger than L2",
             },
             "roofline": {
                 "kernel": "attention_bwd (tcgen05, per launch = one layer of one micro-batch)",
-                "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16_tflops"], "peak_source": peaks["source"] + " (burst bf16)",
-                "traffic": None,
+                "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops_sustained"],
+                "peak_source": peaks["source"] + " (sustained bf16: the kernel runs inside a long step)",
+                "traffic": ATTN_BWD_DRAM_BYTES[0] * B / ATTN_BWD_DRAM_BYTES[1],
+                "traffic_source": f"ncu dram__bytes_read+write of one launch at B={ATTN_BWD_DRAM_BYTES[1]}, "
+                                  f"scaled by B={B}",
                 "algorithmic_flops_per_launch": bwd_flops,
+                "algorithmic_bytes_per_launch": attn_bwd_bytes,
             },
             "mfu": mfu,
             "kernels": kernels,

@@ -128,6 +128,22 @@ MT_API int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const vo
                         void* workspace, int64_t workspace_bytes, int64_t rows,
                         int64_t dim, void* stream);
 
+/* mt_add_rms_norm_bwd that also writes grad_input rounded to gnorm_dtype into
+ * grad_branch ([rows, dim]).  For a wide residual stream (fp32 new_residual and
+ * grad_input) feeding a narrower branch (bf16 hidden): both add inputs take the
+ * same gradient, one per dtype, from one pass.  No counterpart kernel in the
+ * reference, where autocast casts the shared gradient in a separate op
+ * (residual adds of src/mega_trading/model.py:185-186 under the autocast of
+ * trainer.py:336). */
+MT_API int mt_add_rms_norm_bwd_dual(const void* new_residual, int res_dtype, const void* w,
+                             int w_dtype, const float* rstd,
+                             const void* grad_new_residual, int gres_dtype,
+                             const void* grad_normed, int gnorm_dtype,
+                             void* grad_input, int gin_dtype, void* grad_branch,
+                             void* dw, int dw_dtype, void* workspace,
+                             int64_t workspace_bytes, int64_t rows, int64_t dim,
+                             void* stream);
+
 /* ---------------------------------------------------------------------
  * RoPE (interleaved pairs)   replaces triton_apply_rope
  *   (src/mega_trading/kernels/triton_ops.py:45-54, _launch_rope_kernel

@@ -49,6 +49,11 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_i64, c_i64,
          c_i64, c_vp],
     ),
+    "mt_add_rms_norm_bwd_dual": (
+        c_int,
+        [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_i64,
+         c_i64, c_i64, c_vp],
+    ),
     "mt_rope": (
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p,

@@ -144,7 +144,8 @@ template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool
 __global__ void __launch_bounds__(kWarps * 32, (NC <= 4 ? 3 : 1))
     rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rstd,
                 const TG* __restrict__ dy, const TGR* __restrict__ gres, TD* __restrict__ dx,
-                float* __restrict__ partial, int64_t rows, int dim) {
+                TG* __restrict__ dx2, float* __restrict__ partial, int64_t rows, int dim) {
+  // dx2 (optional): dx once more, rounded to dy's dtype
   extern __shared__ float red[];  // [kWarps][dim]
   const int lane = lane_id();
   const int warp = warp_id();
@@ -189,6 +190,7 @@ __global__ void __launch_bounds__(kWarps * 32, (NC <= 4 ? 3 : 1))
           acc[c][i] = fmaf(gv[i], xv[i] * inv, acc[c][i]);
         }
         store8<TD>(dx + row * dim + col, o);
+        if (dx2 != nullptr) store8<TG>(dx2 + row * dim + col, o);
       }
     }
   }
@@ -214,8 +216,8 @@ template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool
 __global__ void __launch_bounds__(kWarps * 32) rms_bwd_scalar(const TX* __restrict__ x, const TW* __restrict__ w,
                                                               const float* __restrict__ rstd,
                                                               const TG* __restrict__ dy, const TGR* __restrict__ gres,
-                                                              TD* __restrict__ dx, float* __restrict__ partial,
-                                                              int64_t rows, int dim) {
+                                                              TD* __restrict__ dx, TG* __restrict__ dx2,
+                                                              float* __restrict__ partial, int64_t rows, int dim) {
   // dW partial per block: thread t owns columns t, t + blockDim, ... and
   // loops over the block's rows itself (no cross-warp reduction needed).
   for (int col = threadIdx.x; col < dim; col += blockDim.x) {
@@ -236,6 +238,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_scalar(const TX* __restri
       float o = inv * (to_f32<TG>(dy[row * dim + col]) * to_f32<TW>(w[col]) - to_f32<TX>(x[row * dim + col]) * k);
       if constexpr (GRES) o += to_f32<TGR>(gres[row * dim + col]);
       dx[row * dim + col] = from_f32<TD>(o);
+      if (dx2 != nullptr) dx2[row * dim + col] = from_f32<TG>(o);
     }
   }
 }
@@ -322,19 +325,20 @@ int bwd_blocks(int64_t rows) {
 template <bool GRES, typename TX, typename TW, typename TG, typename TGR, typename TD, typename TDW>
 int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* gres, void* dx, void* dw,
                void* workspace, int64_t ws_bytes, int64_t rows, int64_t dim, cudaStream_t stream,
-               int max_blocks = 0) {
+               int max_blocks = 0, void* dx2 = nullptr) {
   int nblocks = bwd_blocks(rows);
   if (max_blocks > 0 && nblocks > max_blocks) nblocks = max_blocks;
   if (workspace == nullptr || ws_bytes < int64_t(nblocks) * dim * 4) return MT_ERR_WORKSPACE;
   float* partial = static_cast<float*>(workspace);
   const int nc = chunks_for(dim);
   const bool vec = nc > 0 && dim % kChunk == 0 && aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dx) &&
-                   (!GRES || aligned16(gres));
+                   (!GRES || aligned16(gres)) && (dx2 == nullptr || aligned16(dx2));
   auto X = static_cast<const TX*>(x);
   auto W = static_cast<const TW*>(w);
   auto G = static_cast<const TG*>(dy);
   auto GR = static_cast<const TGR*>(gres);
   auto DX = static_cast<TD*>(dx);
+  auto DX2 = static_cast<TG*>(dx2);
   const int d = (int)dim;
   const int smem = kWarps * d * 4;
   if (vec) {
@@ -350,15 +354,15 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
     int st = set_smem_limit(fn, smem);
     if (st != MT_OK) return st;
     switch (nc) {
-      case 1: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
-      case 2: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
-      case 3: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
-      case 4: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
-      case 6: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
-      default: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d); break;
+      case 1: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      case 2: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      case 3: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      case 4: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      case 6: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      default: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
     }
   } else {
-    rms_bwd_scalar<TX, TW, TG, TGR, TD, GRES><<<nblocks, kWarps * 32, 0, stream>>>(X, W, rstd, G, GR, DX, partial, rows, d);
+    rms_bwd_scalar<TX, TW, TG, TGR, TD, GRES><<<nblocks, kWarps * 32, 0, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d);
   }
   int st = check_launch(GRES ? "add_rms_norm_bwd" : "rms_norm_bwd");
   if (st != MT_OK) return st;
@@ -470,10 +474,11 @@ int mt_add_rms_norm_fwd(const void* hidden, const void* residual, int act_dtype,
   }
 }
 
-int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, int w_dtype, const float* rstd,
-                        const void* grad_new_residual, int gres_dtype, const void* grad_normed, int gnorm_dtype,
-                        void* grad_input, int gin_dtype, void* dw, int dw_dtype, void* workspace,
-                        int64_t workspace_bytes, int64_t rows, int64_t dim, void* stream) {
+static int add_rms_norm_bwd_impl(const void* new_residual, int res_dtype, const void* w, int w_dtype,
+                                 const float* rstd, const void* grad_new_residual, int gres_dtype,
+                                 const void* grad_normed, int gnorm_dtype, void* grad_input, int gin_dtype,
+                                 void* grad_branch, void* dw, int dw_dtype, void* workspace, int64_t workspace_bytes,
+                                 int64_t rows, int64_t dim, void* stream) {
   int st = validate_rows(new_residual, grad_input, rows, dim);
   if (st != MT_OK) return st;
   auto s = static_cast<cudaStream_t>(stream);
@@ -484,7 +489,8 @@ int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, 
 #define CASE(a, b, c, d, e, f, TA, TB, TC, TD, TE, TF)                                                          \
   case key5(a, b, c, d, e) | (f << 10):                                                                          \
     return launch_bwd<true, TA, TB, TC, TE, TF, TD>(new_residual, w, rstd, grad_normed, grad_new_residual,       \
-                                                    grad_input, dw, workspace, workspace_bytes, rows, dim, s);
+                                                    grad_input, dw, workspace, workspace_bytes, rows, dim, s, 0, \
+                                                    grad_branch);
     CASE(MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, MT_BF16, bf, bf, bf, bf, bf, bf)
     CASE(MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, MT_F16, hf, hf, hf, hf, hf, hf)
     CASE(MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, MT_F32, float, float, float, float, float, float)
@@ -493,6 +499,25 @@ int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, 
 #undef CASE
     default: return MT_ERR_UNSUPPORTED_DTYPE;
   }
+}
+
+int mt_add_rms_norm_bwd(const void* new_residual, int res_dtype, const void* w, int w_dtype, const float* rstd,
+                        const void* grad_new_residual, int gres_dtype, const void* grad_normed, int gnorm_dtype,
+                        void* grad_input, int gin_dtype, void* dw, int dw_dtype, void* workspace,
+                        int64_t workspace_bytes, int64_t rows, int64_t dim, void* stream) {
+  return add_rms_norm_bwd_impl(new_residual, res_dtype, w, w_dtype, rstd, grad_new_residual, gres_dtype, grad_normed,
+                               gnorm_dtype, grad_input, gin_dtype, nullptr, dw, dw_dtype, workspace, workspace_bytes,
+                               rows, dim, stream);
+}
+
+int mt_add_rms_norm_bwd_dual(const void* new_residual, int res_dtype, const void* w, int w_dtype, const float* rstd,
+                             const void* grad_new_residual, int gres_dtype, const void* grad_normed, int gnorm_dtype,
+                             void* grad_input, int gin_dtype, void* grad_branch, void* dw, int dw_dtype,
+                             void* workspace, int64_t workspace_bytes, int64_t rows, int64_t dim, void* stream) {
+  if (grad_branch == nullptr && rows > 0) return MT_ERR_INVALID_ARGUMENT;
+  return add_rms_norm_bwd_impl(new_residual, res_dtype, w, w_dtype, rstd, grad_new_residual, gres_dtype, grad_normed,
+                               gnorm_dtype, grad_input, gin_dtype, grad_branch, dw, dw_dtype, workspace,
+                               workspace_bytes, rows, dim, stream);
 }
 
 }  // extern "C"

@@ -56,11 +56,13 @@ def _rms_fwd(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtyp
     return y, rstd
 
 
-def _rms_bwd(x, w, rstd, dy, dx_dtype, residual_grad=None):
+def _rms_bwd(x, w, rstd, dy, dx_dtype, residual_grad=None, branch_dtype=None):
+    """dx (and dw); with ``branch_dtype`` also dx rounded to that dtype, written by the same kernel."""
     lib = _lib.load()
     dim = x.shape[-1]
     rows = x.numel() // dim
     dx = torch.empty(x.shape, device=x.device, dtype=dx_dtype)
+    dx2 = None
     dw = torch.empty(w.shape, device=w.device, dtype=w.dtype)
     ws_bytes = int(lib.mt_rms_norm_bwd_workspace_bytes(rows, dim))
     ws = torch.empty((max(ws_bytes, 4),), device=x.device, dtype=torch.uint8)
@@ -71,7 +73,7 @@ def _rms_bwd(x, w, rstd, dy, dx_dtype, residual_grad=None):
             _lib.dtype_code(w.dtype), ws.data_ptr(), ws.numel(), rows, dim, _dev_stream(x),
         )
         _lib.check(st, "rms_norm backward")
-    else:
+    elif branch_dtype is None or branch_dtype == dx_dtype:
         st = lib.mt_add_rms_norm_bwd(
             x.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), _lib.dtype_code(w.dtype), rstd.data_ptr(),
             residual_grad.data_ptr(), _lib.dtype_code(residual_grad.dtype), dy.data_ptr(), _lib.dtype_code(dy.dtype),
@@ -79,7 +81,20 @@ def _rms_bwd(x, w, rstd, dy, dx_dtype, residual_grad=None):
             ws.numel(), rows, dim, _dev_stream(x),
         )
         _lib.check(st, "add_rms_norm backward")
+    else:
+        if branch_dtype != dy.dtype:
+            raise ValueError("the branch gradient takes the dtype of the normalised-output gradient")
+        dx2 = torch.empty(x.shape, device=x.device, dtype=branch_dtype)
+        st = lib.mt_add_rms_norm_bwd_dual(
+            x.data_ptr(), _lib.dtype_code(x.dtype), w.data_ptr(), _lib.dtype_code(w.dtype), rstd.data_ptr(),
+            residual_grad.data_ptr(), _lib.dtype_code(residual_grad.dtype), dy.data_ptr(), _lib.dtype_code(dy.dtype),
+            dx.data_ptr(), _lib.dtype_code(dx_dtype), dx2.data_ptr(), dw.data_ptr(), _lib.dtype_code(w.dtype),
+            ws.data_ptr(), ws.numel(), rows, dim, _dev_stream(x),
+        )
+        _lib.check(st, "add_rms_norm backward (dual)")
     _lib.count(2)
+    if branch_dtype is not None:
+        return dx, dw, (dx if dx2 is None else dx2)
     return dx, dw
 
 
@@ -146,10 +161,15 @@ class _AddRMSNorm(torch.autograd.Function):
             grad_new_residual = torch.zeros_like(new_res)
         if grad_normed is None:
             grad_normed = torch.zeros(new_res.shape, device=new_res.device, dtype=new_res.dtype)
-        dx, dw = _rms_bwd(new_res, w, rstd, grad_normed.contiguous(), new_res.dtype,
-                          residual_grad=grad_new_residual.to(new_res.dtype).contiguous())
-        # both add inputs receive the same gradient (triton_ops.py:288-291)
-        dh = dx if ctx.hidden_dtype == dx.dtype else dx.to(ctx.hidden_dtype)
+        gn = grad_normed.contiguous()
+        # both add inputs receive the same gradient (triton_ops.py:288-291); a
+        # narrower hidden dtype gets its rounded copy from the same kernel
+        branch = ctx.hidden_dtype if ctx.hidden_dtype == gn.dtype else None
+        dx, dw, dh = _rms_bwd(new_res, w, rstd, gn, new_res.dtype,
+                              residual_grad=grad_new_residual.to(new_res.dtype).contiguous(),
+                              branch_dtype=branch or new_res.dtype)
+        if dh.dtype != ctx.hidden_dtype:
+            dh = dh.to(ctx.hidden_dtype)
         return dh, dx, dw, None, None
 
 

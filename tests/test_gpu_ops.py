@@ -77,6 +77,33 @@ def test_rms_norm_mixed_fp32_residual_bf16_out(cuda_device):
     _check(wd.grad, wo.grad, "rms_norm mixed dw")
 
 
+@pytest.mark.parametrize("rows,dim", [(4096, 768), (37, 768), (5, 200)])
+def test_add_rms_norm_mixed_dual_gradient(cuda_device, rows, dim):
+    """bf16 branch + fp32 residual stream: the fp32 gradient and its bf16 copy come from one kernel."""
+    from mega_trading_b200.kernels import triton_ops as K
+
+    g = torch.Generator().manual_seed(rows + dim)
+    x = torch.randn(rows, dim, generator=g)
+    r = torch.randn(rows, dim, generator=g)
+    w = 1 + 0.1 * torch.randn(dim, generator=g)
+    gres = torch.randn(rows, dim, generator=g)
+    gnorm = torch.randn(rows, dim, generator=g)
+    xd = _leaf(x, cuda_device, torch.bfloat16)
+    rd, wd = _leaf(r, cuda_device, torch.float32), _leaf(w, cuda_device, torch.float32)
+    new_res, normed = K.add_rms_norm(xd, rd, wd, eps=1e-5, out_dtype=torch.bfloat16)
+    assert new_res.dtype == torch.float32 and normed.dtype == torch.bfloat16
+    torch.autograd.backward([new_res, normed], [gres.to(cuda_device), gnorm.to(cuda_device, torch.bfloat16)])
+    assert xd.grad.dtype == torch.bfloat16 and rd.grad.dtype == torch.float32
+    assert torch.equal(xd.grad, rd.grad.to(torch.bfloat16))  # same values, rounded once
+    xo = x.to(torch.bfloat16).float().requires_grad_(True)
+    ro, wo = r.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    nro, no = O.add_rms_norm(xo, ro, wo, 1e-5)
+    torch.autograd.backward([nro, no], [gres, gnorm.to(torch.bfloat16).float()])
+    _check(normed, no, "dual normed")
+    _check(rd.grad, ro.grad, "dual d_residual")
+    _check(wd.grad, wo.grad, "dual dw")
+
+
 @pytest.mark.parametrize("shape,dtype,seed", [((2, 512, 1024), torch.bfloat16, 37), ((5, 33, 768), torch.float16, 8),
                                               ((16, 768), torch.float32, 9)])
 def test_add_rms_norm_matches_oracle(cuda_device, shape, dtype, seed):
