@@ -214,6 +214,26 @@ MT_API int mt_attention_bwd(const void* q, const void* k, const void* v,
                      void* workspace, int64_t workspace_bytes, uint32_t* status,
                      void* stream);
 
+/* mt_attention_bwd with the RoPE backward folded in: q and k are the ROTATED
+ * query/key the forward consumed, and dq / dk come back as the gradients of
+ * the un-rotated query/key (interleaved-pair RoPE of
+ * src/mega_trading/model.py:286-316, run backwards).  Each dq / dk row is
+ * rotated by -theta(t) in fp32 before its one rounding, so no rotated-gradient
+ * tensor is written.  rope_cos / rope_sin: [T, D/2] tables in dtype with row
+ * stride rope_ld (a multiple of 4 elements, pointers 8-byte aligned).  No
+ * counterpart entry in the reference, which runs triton_apply_rope's backward
+ * as a separate kernel (kernels/triton_ops.py:187-214). */
+MT_API int mt_attention_rope_bwd(const void* q, const void* k, const void* v,
+                          const void* o, const float* lse, const void* dout,
+                          void* dq, void* dk, void* dv, int dtype, int64_t B,
+                          int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                          const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                          const int64_t* os, const int64_t* dos, const int64_t* dqs,
+                          const int64_t* dks, const int64_t* dvs, float scale,
+                          const void* rope_cos, const void* rope_sin, int64_t rope_ld,
+                          void* workspace, int64_t workspace_bytes, uint32_t* status,
+                          void* stream);
+
 
 /* ---------------------------------------------------------------------
  * Fused linear + cross-entropy   replaces triton_fused_linear_cross_entropy

@@ -74,6 +74,12 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p,
          c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_float, c_vp, c_i64, c_vp, c_vp],
     ),
+    "mt_attention_rope_bwd": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p,
+         c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, c_float, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp,
+         c_vp],
+    ),
     "mt_fused_ce_workspace_bytes": (c_i64, [c_i64, c_i64]),
     "mt_fused_ce_fwd": (
         c_int,

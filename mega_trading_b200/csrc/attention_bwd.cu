@@ -86,6 +86,11 @@ struct BwdParams {
   int T, Tp, Hq, Hkv, repeats, n_tiles;
   int n_heads;  // B * Hkv
   int group;    // (batch, kv head) pairs whose key tiles are interleaved in launch order
+  // optional RoPE tables [T, D/2] (row stride rope_ld): dk is rotated back by
+  // -theta(key) before rounding, giving the gradient of the un-rotated keys
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_ld;
   float scale_log2, scale;
   uint32_t* status;
 };
@@ -103,6 +108,25 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// Inverse RoPE of 8 consecutive features (4 interleaved pairs starting at pair
+// index i0) of position t: (e, o) -> (e cos + o sin, o cos - e sin), the
+// transpose of the forward rotation, with the 16-bit tables the forward used.
+template <typename T>
+__device__ __forceinline__ void rope_back8(float (&g)[8], const void* cos_t, const void* sin_t, int64_t ld, int t,
+                                           int i0) {
+  const uint2 cr = *reinterpret_cast<const uint2*>(static_cast<const T*>(cos_t) + int64_t(t) * ld + i0);
+  const uint2 sr = *reinterpret_cast<const uint2*>(static_cast<const T*>(sin_t) + int64_t(t) * ld + i0);
+  const T* ce = reinterpret_cast<const T*>(&cr);
+  const T* se = reinterpret_cast<const T*>(&sr);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float cs = to_f32<T>(ce[i]), sn = to_f32<T>(se[i]);
+    const float e = g[2 * i], od = g[2 * i + 1];
+    g[2 * i] = e * cs + od * sn;
+    g[2 * i + 1] = od * cs - e * sn;
+  }
 }
 
 // Write 32 consecutive query columns (col0 .. col0+31, col0 % 32 == 0) of one
@@ -516,10 +540,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           a.y = pack2<T>(__uint_as_float(vv[q * 8 + 2]), __uint_as_float(vv[q * 8 + 3]));
           a.z = pack2<T>(__uint_as_float(vv[q * 8 + 4]), __uint_as_float(vv[q * 8 + 5]));
           a.w = pack2<T>(__uint_as_float(vv[q * 8 + 6]), __uint_as_float(vv[q * 8 + 7]));
-          c.x = pack2<T>(__uint_as_float(kv[q * 8 + 0]) * p.scale, __uint_as_float(kv[q * 8 + 1]) * p.scale);
-          c.y = pack2<T>(__uint_as_float(kv[q * 8 + 2]) * p.scale, __uint_as_float(kv[q * 8 + 3]) * p.scale);
-          c.z = pack2<T>(__uint_as_float(kv[q * 8 + 4]) * p.scale, __uint_as_float(kv[q * 8 + 5]) * p.scale);
-          c.w = pack2<T>(__uint_as_float(kv[q * 8 + 6]) * p.scale, __uint_as_float(kv[q * 8 + 7]) * p.scale);
+          float g[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[i] = __uint_as_float(kv[q * 8 + i]) * p.scale;
+          if (p.rope_cos != nullptr) rope_back8<T>(g, p.rope_cos, p.rope_sin, p.rope_ld, key, (wg * kCols + q * 8) / 2);
+          c.x = pack2<T>(g[0], g[1]);
+          c.y = pack2<T>(g[2], g[3]);
+          c.z = pack2<T>(g[4], g[5]);
+          c.w = pack2<T>(g[6], g[7]);
           *reinterpret_cast<uint4*>(dvrow + q * 8) = a;
           *reinterpret_cast<uint4*>(dkrow + q * 8) = c;
         }
@@ -572,10 +600,12 @@ __global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, con
 }
 
 // postprocess: dq[b,h,t,:] = scale * dq_acc[row, :]
+// (with RoPE tables: rotated back by -theta(t) before rounding)
 template <typename T, int D>
 __global__ void __launch_bounds__(256) attn_bwd_post(const float* __restrict__ acc, T* __restrict__ dq,
                                                      int64_t s0, int64_t s1, int64_t s2, int Hq, int seq, int Tp,
-                                                     float scale, int64_t rows) {
+                                                     float scale, int64_t rows, const void* rope_cos,
+                                                     const void* rope_sin, int64_t rope_ld) {
   constexpr int LPR = D / 8;
   const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t row = gid / LPR;
@@ -587,8 +617,9 @@ __global__ void __launch_bounds__(256) attn_bwd_post(const float* __restrict__ a
   const int b = (int)(bh / Hq), h = (int)(bh - int64_t(b) * Hq);
   const float4* src = reinterpret_cast<const float4*>(acc + row * D + sub * 8);
   const float4 x = src[0], y = src[1];
-  const float v[8] = {x.x * scale, x.y * scale, x.z * scale, x.w * scale,
-                      y.x * scale, y.y * scale, y.z * scale, y.w * scale};
+  float v[8] = {x.x * scale, x.y * scale, x.z * scale, x.w * scale,
+                y.x * scale, y.y * scale, y.z * scale, y.w * scale};
+  if (rope_cos != nullptr) rope_back8<T>(v, rope_cos, rope_sin, rope_ld, t, sub * 4);
   store_vec<T, 8>(dq + b * s0 + h * s1 + int64_t(t) * s2 + sub * 8, v);
 }
 
@@ -649,7 +680,8 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
   {
     const int64_t threads = rows * (D / 8);
     attn_bwd_post<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        ws.dq_acc, static_cast<T*>(dq), dqs[0], dqs[1], dqs[2], prm.Hq, prm.T, prm.Tp, prm.scale, rows);
+        ws.dq_acc, static_cast<T*>(dq), dqs[0], dqs[1], dqs[2], prm.Hq, prm.T, prm.Tp, prm.scale, rows,
+        prm.rope_cos, prm.rope_sin, prm.rope_ld);
     return check_launch("attention_bwd_post");
   }
 }
@@ -664,12 +696,13 @@ extern "C" int64_t mt_attention_bwd_workspace_bytes(int64_t B, int64_t Hq, int64
   return carve(nullptr, B, Hq, T, D).bytes;
 }
 
-extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
-                                const void* dout, void* dq, void* dk, void* dv, int dtype, int64_t B, int64_t Hq,
-                                int64_t Hkv, int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
-                                const int64_t* vs, const int64_t* os, const int64_t* dos, const int64_t* dqs,
-                                const int64_t* dks, const int64_t* dvs, float scale, void* workspace,
-                                int64_t workspace_bytes, uint32_t* status, void* stream) {
+static int attention_bwd_impl(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                              const void* dout, void* dq, void* dk, void* dv, int dtype, int64_t B, int64_t Hq,
+                              int64_t Hkv, int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
+                              const int64_t* vs, const int64_t* os, const int64_t* dos, const int64_t* dqs,
+                              const int64_t* dks, const int64_t* dvs, float scale, const void* rope_cos,
+                              const void* rope_sin, int64_t rope_ld, void* workspace, int64_t workspace_bytes,
+                              uint32_t* status, void* stream) {
   if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || (Hq % Hkv) != 0) return MT_ERR_INVALID_ARGUMENT;
   if (D != 64 && D != 32) return MT_ERR_INVALID_ARGUMENT;
@@ -713,6 +746,9 @@ extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, con
   prm.delta = ws.delta;
   prm.dk = dk;
   prm.dv = dv;
+  prm.rope_cos = rope_cos;
+  prm.rope_sin = rope_sin;
+  prm.rope_ld = rope_ld;
   for (int i = 0; i < 4; ++i) {
     prm.dks[i] = dks[i];
     prm.dvs[i] = dvs[i];
@@ -735,4 +771,30 @@ extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, con
               : run_bwd<__half, 64>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s);
   return bf ? run_bwd<__nv_bfloat16, 32>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s)
             : run_bwd<__half, 32>(prm, o, dout, lse, dq, os, dos, dqs, ws, b, s);
+}
+
+extern "C" int mt_attention_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                                const void* dout, void* dq, void* dk, void* dv, int dtype, int64_t B, int64_t Hq,
+                                int64_t Hkv, int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
+                                const int64_t* vs, const int64_t* os, const int64_t* dos, const int64_t* dqs,
+                                const int64_t* dks, const int64_t* dvs, float scale, void* workspace,
+                                int64_t workspace_bytes, uint32_t* status, void* stream) {
+  return attention_bwd_impl(q, k, v, o, lse, dout, dq, dk, dv, dtype, B, Hq, Hkv, T, D, qs, ks, vs, os, dos, dqs, dks,
+                            dvs, scale, nullptr, nullptr, 0, workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int mt_attention_rope_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                                     const void* dout, void* dq, void* dk, void* dv, int dtype, int64_t B,
+                                     int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* qs,
+                                     const int64_t* ks, const int64_t* vs, const int64_t* os, const int64_t* dos,
+                                     const int64_t* dqs, const int64_t* dks, const int64_t* dvs, float scale,
+                                     const void* rope_cos, const void* rope_sin, int64_t rope_ld, void* workspace,
+                                     int64_t workspace_bytes, uint32_t* status, void* stream) {
+  if (rope_cos == nullptr || rope_sin == nullptr || rope_ld < D / 2) return MT_ERR_INVALID_ARGUMENT;
+  // 8-byte table reads: 4 pairs at a time
+  if ((reinterpret_cast<uintptr_t>(rope_cos) & 7u) || (reinterpret_cast<uintptr_t>(rope_sin) & 7u) ||
+      (rope_ld % 4) != 0)
+    return MT_ERR_UNSUPPORTED_LAYOUT;
+  return attention_bwd_impl(q, k, v, o, lse, dout, dq, dk, dv, dtype, B, Hq, Hkv, T, D, qs, ks, vs, os, dos, dqs, dks,
+                            dvs, scale, rope_cos, rope_sin, rope_ld, workspace, workspace_bytes, status, stream);
 }

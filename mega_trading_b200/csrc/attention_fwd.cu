@@ -104,11 +104,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
 
-  const int bh = blockIdx.x;
-  const int b = bh / p.Hq;
-  const int h = bh - b * p.Hq;
-  const int hk = h / p.repeats;
-  const int pair = p.n_pairs - 1 - (int)blockIdx.y;  // heaviest pair first
+  // Launch order: one (batch, kv head) after another; inside it the query-tile
+  // pairs go heaviest first, and the `repeats` query heads of one pair are
+  // adjacent.  Every CTA that streams a kv head's K/V tiles is then resident
+  // at about the same time, so those tiles come from DRAM about once.
+  const int per_kv = p.n_pairs * p.repeats;
+  const int bk = (int)blockIdx.x / per_kv;
+  const int rem = (int)blockIdx.x - bk * per_kv;
+  const int pi = rem / p.repeats;
+  const int b = bk / p.Hkv;
+  const int hk = bk - b * p.Hkv;
+  const int h = hk * p.repeats + (rem - pi * p.repeats);
+  const int pair = p.n_pairs - 1 - pi;  // heaviest pair first
   // slot s handles query tile 2*pair + s; it sees key tiles 0..(2*pair + s)
   const bool active1 = (2 * pair + 1) < p.n_qtiles;
   const int nkv0 = 2 * pair + 1;
@@ -392,8 +399,9 @@ int launch_fwd(const FwdParams& prm, int B, int Hq, cudaStream_t stream) {
   auto kern = attn_fwd_kernel<T, D>;
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
-  dim3 grid((unsigned)(B * Hq), (unsigned)prm.n_pairs);
-  kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
+  const int64_t blocks = int64_t(B) * Hq * prm.n_pairs;
+  if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+  kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
   return check_launch("attention_fwd");
 }
 

@@ -6,7 +6,8 @@ applies RoPE to the q/k slices, runs causal GQA attention and returns O in the
 ``[B, T, Hq, D]`` physical layout (so ``O.transpose(1, 2).reshape(B, T, H)`` is
 free).  Its backward writes dq, dk and dv straight into one packed
 ``[B, T, (Hq + 2 Hkv) D]`` gradient through strided views, so the backward of
-the projection is again ONE GEMM and no gradient slices are copied or added.
+the projection is again ONE GEMM and no gradient slices are copied or added;
+the RoPE backward is folded into the attention backward's dq / dk epilogues.
 Same math as the reference's q/k/v projections + ``RotaryEmbedding`` +
 ``triton_attention`` (``src/mega_trading/model.py:218-237, 286-294``).
 
@@ -61,10 +62,8 @@ class _QKVRopeAttention(torch.autograd.Function):
         do = _attn._aligned_view(grad_o)
         dqkv = torch.empty((B, T, (hq + 2 * hkv) * d), device=q_rot.device, dtype=q_rot.dtype)
         dq, dk, dv = _split(dqkv, hq, hkv, d)
-        dq_rot = _bthd(B, T, hq, d, q_rot)
-        dk_rot = _bthd(B, T, hkv, d, q_rot)
-        _attn._launch_bwd(q_rot, k_rot, v, o, lse, do, ctx.scale, dq=dq_rot, dk=dk_rot, dv=dv)
-        _ops._launch_rope(dq_rot, dk_rot, cos, sin, dq, dk, negate=True)
+        # the RoPE backward runs inside the attention backward's dq / dk epilogues
+        _attn._launch_bwd(q_rot, k_rot, v, o, lse, do, ctx.scale, dq=dq, dk=dk, dv=dv, rope=(cos, sin))
         return dqkv, None, None, None, None, None
 
 

@@ -40,7 +40,9 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     return o, lse
 
 
-def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None):
+def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None, rope=None):
+    """Attention backward; with ``rope=(cos, sin)`` ([T, D/2] tables in q's dtype) q / k are the
+    rotated inputs and dq / dk come back as the gradients of the un-rotated ones."""
     lib = _lib.load()
     B, Hq, T, D = q.shape
     Hkv = k.shape[1]
@@ -51,14 +53,21 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None):
     ws = torch.empty((max(ws_bytes, 16),), device=q.device, dtype=torch.uint8)
     status = _lib.status_word(q.device)
     tok = _lib.timer.start("attention_bwd", q.device)
-    st = lib.mt_attention_bwd(
+    common = (
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(), dq.data_ptr(),
         dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), B, Hq, Hkv, T, D,
         _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
         _lib.i64_array(o.stride()), _lib.i64_array(do.stride()), _lib.i64_array(dq.stride()),
-        _lib.i64_array(dk.stride()), _lib.i64_array(dv.stride()), float(scale), ws.data_ptr(), ws.numel(),
-        status.data_ptr(), _lib.stream_ptr(q.device),
+        _lib.i64_array(dk.stride()), _lib.i64_array(dv.stride()), float(scale),
     )
+    tail = (ws.data_ptr(), ws.numel(), status.data_ptr(), _lib.stream_ptr(q.device))
+    if rope is None:
+        st = lib.mt_attention_bwd(*common, *tail)
+    else:
+        cos, sin = rope
+        if cos.dtype != q.dtype or sin.dtype != q.dtype or cos.stride(-1) != 1 or sin.stride() != cos.stride():
+            raise ValueError("RoPE tables must be [T, D/2] in the query dtype with unit inner stride")
+        st = lib.mt_attention_rope_bwd(*common, cos.data_ptr(), sin.data_ptr(), cos.stride(0), *tail)
     _lib.timer.stop(tok)
     _lib.check(st, "attention backward")
     _lib.count(3)
