@@ -35,9 +35,9 @@ SEQ = 2048
 MICRO_BATCH = 128
 CPU_SAMPLE_SEQS = 1
 # DRAM bytes (read + write) of one attn_bwd_kernel launch measured by ncu at
-# B=32, Hq=12, Hkv=4, T=2048, D=64 (profiles/attention_bwd_config3_layer.txt);
-# traffic grows with the batch, so a launch of B sequences moves B/32 times this.
-ATTN_BWD_DRAM_BYTES = (476_131_328 + 225_660_416, 32)
+# B=128, Hq=12, Hkv=4, T=2048, D=64 (profiles/attention_bwd_config3_layer.txt);
+# traffic grows with the batch, so a launch of B sequences moves B/128 times this.
+ATTN_BWD_DRAM_BYTES = (1_904_392_192 + 1_030_479_616, 128)
 
 
 def _peaks() -> dict:
@@ -301,7 +301,8 @@ def main(argv: list[str] | None = None) -> int:
                       "is far larger than L2",
             },
             "roofline": {
-                "kernel": "attention_bwd (tcgen05, per launch = one layer of one micro-batch)",
+                "kernel": "attention_bwd (tcgen05, per launch = one layer of one micro-batch; CUDA events "
+                          "around the whole call: dQ-accumulator clear, pre, main and post kernels)",
                 "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"] + " (sustained bf16: the kernel runs inside a long step)",
