@@ -40,6 +40,10 @@ constexpr int kBM = 128;  // query rows per slot
 constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 2;  // query tiles per CTA (consecutive tiles of one head)
 constexpr int kThreads = 320;
+// Of every 8 pairs of scores, kPolyPairs take the polynomial exp2 on the FMA
+// pipe and the rest the MUFU ex2 (16 per clock per SM), the forward's
+// bottleneck at D=64: measured best at 1 (603 vs 584 TFLOP/s at T=4096).
+constexpr int kPolyPairs = 1;
 constexpr uint32_t kKernelId = 1;
 
 template <int D>
@@ -100,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bar_s_full = bar_kv_empty + C::NST;  // [kSlots]
   uint64_t* bar_s_free = bar_s_full + kSlots;    // [kSlots]
   uint64_t* bar_p_full = bar_s_free + kSlots;    // [kSlots]
-  uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots]
+  uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots] (+1: final MMA drain)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
 
@@ -281,25 +285,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tc_fence_before();
       mbar_arrive(&bar_s_free[slot]);
 
-      // Row max of the raw scores in 8 independent chains; the causal mask
-      // only exists on the diagonal tile (warp-uniform branch).
+      // Row max of the raw scores in 8 independent chains (three-input max:
+      // two new scores per instruction); the causal mask only exists on the
+      // diagonal tile (warp-uniform branch).
       const bool diag = (j == nkv - 1);
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
       if (diag) {
         const int lim = qrow - j * kBN;  // keys 0..lim of this tile are visible
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
+        for (int c = 0; c < kBN; ++c)
           if (c > lim) sv[c] = __float_as_uint(-INFINITY);
-          mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c]));
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sv[c]));
       }
-      const float mx2 = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sv[i]);
+#pragma unroll
+      for (int c = 8; c < kBN; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], __uint_as_float(sv[c + i]), __uint_as_float(sv[c + 8 + i]));
+      }
+      const float mx2 = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
                         p.scale_log2;
       // Lazy rescaling: the running reference max m (log2 units) only moves
       // when the tile max exceeds it by more than 8, so P <= 2^8 and O is
@@ -309,10 +313,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mx2);
         m = mx2;
       }
-      const float neg_m = -m;
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 nm2 = make_float2(-m, -m);
+
+      // P = exp2(s * scale_log2 - m) rounded to T and packed two per word, all
+      // in registers: this does not touch the P tile, so it overlaps the P V
+      // product of the previous tile.
+      uint32_t pk[kBN / 2];
+      float2 sum4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < kBN; c += 2) {
+        const float2 x = fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+        const float2 e = ((c >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        sum4[(c >> 1) & 3] = add2(sum4[(c >> 1) & 3], e);
+        pk[c >> 1] = pack2<T>(e.x, e.y);
+      }
+      const float2 s01 = add2(add2(sum4[0], sum4[1]), add2(sum4[2], sum4[3]));
+      l = l * alpha + (s01.x + s01.y);
 
       if (j > 0) {
-        // PV of the previous tile must be finished before the P tile is
+        // P V of the previous tile must be finished before the P tile is
         // overwritten and O is rescaled.
         if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (j - 1) & 1, 9))) {
           ok = false;
@@ -320,25 +342,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         tc_fence_after();
       }
-      // P = exp2(s * scale_log2 - m) rounded to T, packed two per column and
-      // stored to this row's TMEM lane (the A operand of the P V product)
-      float sum8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
-#pragma unroll
-      for (int ch = 0; ch < kBN / 32; ++ch) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[ch * 32 + i]), p.scale_log2, neg_m));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[ch * 32 + i + 1]), p.scale_log2, neg_m));
-          sum8[i & 7] += e0;
-          sum8[(i + 1) & 7] += e1;
-          pk[i >> 1] = pack2<T>(e0, e1);
-        }
-        tmem_st16(tP + ch * 16, pk);
-      }
-      l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+      for (int ch = 0; ch < kBN / 32; ++ch) tmem_st16(tP + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[ch * 16]));
       if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
@@ -349,7 +354,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
           tmem_st16(tO + c * 16, ov);
         }
-        tmem_st_wait();
       }
       tmem_st_wait();
       tc_fence_before();

@@ -120,6 +120,13 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return r;
 }
 
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // exp2_poly for two values with packed arithmetic.
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   x.x = fmaxf(x.x, -125.f);
