@@ -39,7 +39,7 @@ namespace {
 constexpr int kBM = 128;  // query rows per slot
 constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 2;  // query tiles per CTA (consecutive tiles of one head)
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;  // 8 softmax warps, 1 TMA warp, 2 MMA warps
 // Of every 8 pairs of scores, kPolyPairs take the polynomial exp2 on the FMA
 // pipe and the rest the MUFU ex2 (16 per clock per SM), the forward's
 // bottleneck at D=64: measured best at 1 (603 vs 584 TFLOP/s at T=4096).
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bar_s_full = bar_kv_empty + C::NST;  // [kSlots]
   uint64_t* bar_s_free = bar_s_full + kSlots;    // [kSlots]
   uint64_t* bar_p_full = bar_s_free + kSlots;    // [kSlots]
-  uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots] (+1: final MMA drain)
+  uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots] (+kSlots: final MMA drains)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
 
@@ -134,11 +134,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(&bar_p_full[s], 128);
       mbar_init(&bar_o_done[s], 1);
     }
-    mbar_init(bar_o_done + kSlots, 1);  // final MMA drain
+    mbar_init(bar_o_done + kSlots, 1);      // final MMA drain, slot 0
+    mbar_init(bar_o_done + kSlots + 1, 1);  // final MMA drain, slot 1
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar_k_full[s], 1);
       mbar_init(&bar_v_full[s], 1);
-      mbar_init(&bar_kv_empty[s], 1);
+      mbar_init(&bar_kv_empty[s], active1 ? 2 : 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -182,8 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp >= 9) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t idesc_s = make_idesc(kBM, kBN, kBf16, 0, 0);
@@ -208,50 +209,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                   (acc_first || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = wait_bounded(wc, &bar_q[0], 0, 2) && (!active1 || wait_bounded(wc, &bar_q[1], 0, 2)) &&
-                wait_bounded(wc, &bar_k_full[0], 0, 3);
+      // One issuing thread per slot: each slot's S(j+1) goes out as soon as
+      // that slot has read S(j), and its P V(j) as soon as it has written
+      // P(j), whatever the other slot is doing.
+      const int slot = warp - 9;
+      const int nkv = slot ? nkv1 : nkv0;
+      bool ok = nkv > 0 && wait_bounded(wc, &bar_q[slot], 0, 2) && wait_bounded(wc, &bar_k_full[0], 0, 3);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        umma_commit(&bar_s_full[0]);
-        if (active1) {
-          issue_s(1, 0);
-          umma_commit(&bar_s_full[1]);
-        }
+        issue_s(slot, 0);
+        umma_commit(&bar_s_full[slot]);
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
+      for (int j = 0; ok && j < nkv; ++j) {
         const int st = j % C::NST;
-        if (j + 1 < n_kv) {
+        if (j + 1 < nkv) {
           const int st1 = (j + 1) % C::NST;
-          if (!wait_bounded(wc, &bar_k_full[st1], ((j + 1) / C::NST) & 1, 4)) break;
-          for (int s = 0; s < kSlots; ++s) {
-            if (j + 1 >= (s ? nkv1 : nkv0)) continue;
-            if (!wait_bounded(wc, &bar_s_free[s], j & 1, 5)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(s, st1);
-            umma_commit(&bar_s_full[s]);
-          }
-          if (!ok) break;
-        }
-        if (!wait_bounded(wc, &bar_v_full[st], (j / C::NST) & 1, 7)) break;
-        for (int s = 0; s < kSlots; ++s) {
-          if (j >= (s ? nkv1 : nkv0)) continue;
-          if (!wait_bounded(wc, &bar_p_full[s], j & 1, 6)) {
-            ok = false;
+          if (!wait_bounded(wc, &bar_k_full[st1], ((j + 1) / C::NST) & 1, 4) ||
+              !wait_bounded(wc, &bar_s_free[slot], j & 1, 5))
             break;
-          }
           tc_fence_after();
-          issue_pv(s, st, j > 0);
-          umma_commit(&bar_o_done[s]);
+          issue_s(slot, st1);
+          umma_commit(&bar_s_full[slot]);
         }
-        if (!ok) break;
-        umma_commit(&bar_kv_empty[st]);
+        if (!wait_bounded(wc, &bar_v_full[st], (j / C::NST) & 1, 7) || !wait_bounded(wc, &bar_p_full[slot], j & 1, 6))
+          break;
+        tc_fence_after();
+        issue_pv(slot, st, j > 0);
+        umma_commit(&bar_o_done[slot]);
+        umma_commit(&bar_kv_empty[st]);  // one arrival per slot that reads this stage
       }
       // every issued MMA completes before TMEM is released (also on abort)
-      uint64_t* bar_fin = bar_o_done + kSlots;
+      uint64_t* bar_fin = bar_o_done + kSlots + slot;
       umma_commit(bar_fin);
       wait_drain(wc, bar_fin, 0, 13);
     }
