@@ -42,8 +42,9 @@ constexpr int kSlots = 2;  // query tiles per CTA (consecutive tiles of one head
 constexpr int kThreads = 352;  // 8 softmax warps, 1 TMA warp, 2 MMA warps
 // Of every 8 pairs of scores, kPolyPairs take the polynomial exp2 on the FMA
 // pipe and the rest the MUFU ex2 (16 per clock per SM), the forward's
-// bottleneck at D=64: measured best at 1 (603 vs 584 TFLOP/s at T=4096).
-constexpr int kPolyPairs = 1;
+// bottleneck at D=64: measured best at 2 (654 vs 646 at 1, 628 at 3 TFLOP/s
+// at T=4096).
+constexpr int kPolyPairs = 2;
 constexpr uint32_t kKernelId = 1;
 
 template <int D>
