@@ -236,6 +236,29 @@ MT_API int mt_attention_rope_bwd(const void* q, const void* k, const void* v,
 
 
 /* ---------------------------------------------------------------------
+ * SwiGLU MLP GEMMs   replace the w1 / w3 projections + triton_swiglu_gate
+ *   forward and the w2 input-gradient GEMM + gate backward of SwiGLU
+ *   (src/mega_trading/model.py:249-256; kernels/triton_ops.py:57-61,
+ *   forward :774-782, backward :799-819).  tcgen05 GEMMs with the gate in
+ *   the epilogue; no counterpart kernel in the reference.
+ * Layout: the gate/up weight w13 [2I, K] and the saved activation gu [M, 2I]
+ *   are interleaved in blocks of 128: rows (columns) 256b .. 256b+127 hold
+ *   w1 (gate) block b, 256b+128 .. 256b+255 hold w3 (up) block b.
+ * Forward:  gu = round(x w13^T);  y = round(round(silu(g)) * u)   [M, I].
+ * Backward: dy = round(dout w2)   (w2t = w2^T [I, H], dout [M, H]);
+ *           dgate = dy u s (1 + g (1 - s)), dup = dy round(g s), s = sigmoid(g),
+ *           written to dgu [M, 2I] in the interleaved layout.
+ * I must be a multiple of 256, K (H) a multiple of 8; 16-bit dtypes; all
+ * tensors contiguous row-major, 16-byte aligned.
+ * ------------------------------------------------------------------- */
+MT_API int mt_swiglu_gemm_fwd(const void* x, const void* w13, void* gu, void* y,
+                       int dtype, int64_t M, int64_t K, int64_t I,
+                       uint32_t* status, void* stream);
+MT_API int mt_swiglu_gemm_bwd(const void* dout, const void* w2t, const void* gu,
+                       void* dgu, int dtype, int64_t M, int64_t H, int64_t I,
+                       uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------
  * Fused linear + cross-entropy   replaces triton_fused_linear_cross_entropy
  *   (src/mega_trading/kernels/triton_ops.py:64-92, :294-411, row kernel
  *    :822-887; torch path :99-112)

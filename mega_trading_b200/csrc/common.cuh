@@ -85,6 +85,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Logistic sigmoid shared by every SwiGLU kernel (one definition, so the
+// standalone and GEMM-epilogue gates round identically).
+// (fast reciprocal: 1 / (1 + e^-x) to ~2 ulp, far below the 16-bit rounding
+// every caller applies to silu).
+__device__ __forceinline__ float sigmoid_f32(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
 // 2^x on the FMA pipe (offloads the MUFU unit in softmax loops).
 // x = n + f with n = round(x), taken from the low mantissa bits of
 // x + 1.5 * 2^23, and |f| <= 1/2; 2^f comes from a degree-3 polynomial whose
@@ -150,6 +156,19 @@ template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, fl
 template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two 16-bit values of a packed word as floats (low half first).
+template <typename T> __device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
+template <> __device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {
+  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w);
+  a = __low2float(h);
+  b = __high2float(h);
+}
+template <> __device__ __forceinline__ void unpack2<__half>(uint32_t w, float& a, float& b) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  a = __low2float(h);
+  b = __high2float(h);
 }
 
 // ---------------------------------------------------------------------------
@@ -274,11 +293,21 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                "r"(smem_u32(src)), "r"(c0), "r"(c1)
                : "memory");
 }
+// Shared-memory tile -> global through a tensor map (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// At most one committed bulk group may still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA, commit, TMEM load/store

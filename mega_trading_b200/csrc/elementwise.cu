@@ -127,7 +127,6 @@ __global__ void __launch_bounds__(kThreads) rope_scalar(RopeArgs a, int64_t unit
 //   dg = dy * u * sigma(g) * (1 + g * (1 - sigma(g)))
 //   du = dy * round_T(silu(g))
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) swiglu_fwd_k(const T* __restrict__ g, const T* __restrict__ u,
@@ -139,7 +138,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_fwd_k(const T* __restrict__ g
     load_vec<T, V>(g + i * V, gv);
     load_vec<T, V>(u + i * V, uv);
 #pragma unroll
-    for (int j = 0; j < V; ++j) o[j] = round_to<T>(gv[j] * sigmoidf_(gv[j])) * uv[j];
+    for (int j = 0; j < V; ++j) o[j] = round_to<T>(gv[j] * sigmoid_f32(gv[j])) * uv[j];
     store_vec<T, V>(y + i * V, o);
   }
   // tail (n % V elements), handled by the first threads of block 0
@@ -147,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_fwd_k(const T* __restrict__ g
     const int64_t i = nvec * V + threadIdx.x;
     if (i < n) {
       const float gv = to_f32<T>(g[i]);
-      y[i] = from_f32<T>(round_to<T>(gv * sigmoidf_(gv)) * to_f32<T>(u[i]));
+      y[i] = from_f32<T>(round_to<T>(gv * sigmoid_f32(gv)) * to_f32<T>(u[i]));
     }
   }
 }
@@ -165,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_bwd_k(const T* __restrict__ g
     load_vec<T, V>(dy + i * V, dv);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const float s = sigmoidf_(gv[j]);
+      const float s = sigmoid_f32(gv[j]);
       og[j] = dv[j] * uv[j] * s * (1.f + gv[j] * (1.f - s));
       ou[j] = dv[j] * round_to<T>(gv[j] * s);
     }
@@ -176,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_bwd_k(const T* __restrict__ g
     const int64_t i = nvec * V + threadIdx.x;
     if (i < n) {
       const float gv = to_f32<T>(g[i]), uv = to_f32<T>(u[i]), dv = to_f32<T>(dy[i]);
-      const float s = sigmoidf_(gv);
+      const float s = sigmoid_f32(gv);
       dg[i] = from_f32<T>(dv * uv * s * (1.f + gv * (1.f - s)));
       du[i] = from_f32<T>(dv * round_to<T>(gv * s));
     }
@@ -198,7 +197,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_packed_fwd_k(const T* __restr
     load_vec<T, V>(gu + r * 2 * inter + c, gv);
     load_vec<T, V>(gu + r * 2 * inter + inter + c, uv);
 #pragma unroll
-    for (int j = 0; j < V; ++j) o[j] = round_to<T>(gv[j] * sigmoidf_(gv[j])) * uv[j];
+    for (int j = 0; j < V; ++j) o[j] = round_to<T>(gv[j] * sigmoid_f32(gv[j])) * uv[j];
     store_vec<T, V>(y + r * inter + c, o);
   }
 }
@@ -217,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) swiglu_packed_bwd_k(const T* __restr
     load_vec<T, V>(dy + r * inter + c, dv);
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const float s = sigmoidf_(gv[j]);
+      const float s = sigmoid_f32(gv[j]);
       og[j] = dv[j] * uv[j] * s * (1.f + gv[j] * (1.f - s));
       ou[j] = dv[j] * round_to<T>(gv[j] * s);
     }

@@ -71,12 +71,6 @@ struct CeParams {
   uint32_t* status;
 };
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1)
-               : "memory");
-}
-
 __device__ __forceinline__ int64_t load_label(const CeParams& p, int row) {
   return p.labels_i64 ? static_cast<const int64_t*>(p.labels)[row] : (int64_t) static_cast<const int32_t*>(p.labels)[row];
 }

@@ -1,0 +1,419 @@
+// SwiGLU MLP projections as tcgen05 GEMMs with the gate fused into their
+// epilogues, for sm_100a.
+//
+// Reference semantics (duoan/mega-trading): SwiGLU.forward
+// src/mega_trading/model.py:249-256 -- w2(silu(w1(x)) * w3(x)) -- with the
+// gate of kernels/triton_ops.py:57-61 (forward :774-782, backward :799-819):
+// the projections are bf16 GEMMs (autocast) whose outputs are rounded to
+// bf16, silu(gate) is rounded to the activation dtype before the product.
+//
+// B200 design
+//   Both kernels are one persistent GEMM C[M, N] = A[M, K] B[N, K]^T (K-major
+//   operands, 128B swizzle) over 128 x 256 tiles: a TMA producer warp streams
+//   64-wide K chunks through an NST-stage ring, one thread issues
+//   tcgen05.mma into one of two 256-column TMEM accumulators, and four
+//   epilogue warps (thread = row = TMEM lane) drain the other accumulator in
+//   32-column steps, so a tile's epilogue overlaps the next tile's MMAs.
+//   Epilogue outputs leave through TMA stores of [128 x 32] 16-bit boxes.
+//
+//   MODE 0 (forward, W1||W3): B is the gate/up weight interleaved in blocks of
+//     128 rows (w1[0:128], w3[0:128], w1[128:256], w3[128:256], ...), so each
+//     256-column tile holds matching gate and up columns.  The epilogue writes
+//     gate and up (rounded to bf16: the saved activation, in the same
+//     interleaved layout) and y = round(round(silu(g)) * u), the W2 input.
+//   MODE 1 (backward, W2 dgrad): A = dOut [M, H], B = W2^T [I, H]; the tile is
+//     dY for 256 gate columns.  A loader warp prefetches the matching gate/up
+//     boxes of the saved activation through a 3-slot ring; the epilogue rounds
+//     dY to bf16 (the GEMM output dtype) and writes dgate / dup in the
+//     interleaved layout: dg = dy u s (1 + g (1 - s)), du = dy round(g s).
+// Warp roles (352 threads): warps 0-7 epilogue in two warpgroups taking
+// alternate 32-column steps (each with its own staging boxes), 8 TMA producer
+// (+ TMEM allocation), 9 MMA issuer, 10 epilogue-input loader (MODE 1).
+#include <algorithm>
+#include <cmath>
+#include <initializer_list>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace mt {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kEC = 32;    // epilogue columns per step
+constexpr int kGB = 128;   // gate / up interleave block
+constexpr int kThreads = 352;
+constexpr uint32_t kKernelId = 6;
+
+template <int MODE>
+struct GCfg {
+  static constexpr int NST = 3;
+  static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
+  static constexpr int B_BYTES = kBN * kBK * 2;  // 32 KB
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int BOX = kBM * kEC * 2;      // [128 rows][32 cols] 16-bit = 8 KB, 64 B rows
+  static constexpr int N_OUT = MODE == 0 ? 3 : 2;
+  static constexpr int E = MODE == 0 ? 0 : 3;    // epilogue-input ring slots (gate + up box each)
+  static constexpr int OFF_OUT = NST * STAGE;    // [2 warpgroups][N_OUT boxes]
+  static constexpr int OFF_IN = OFF_OUT + 2 * N_OUT * BOX;
+  static constexpr int OFF_BAR = OFF_IN + E * 2 * BOX;
+  static constexpr int SMEM = OFF_BAR + 256;
+  static_assert(SMEM <= 227 * 1024, "more shared memory than one sm_100 CTA may use");
+};
+
+struct GemmParams {
+  CUtensorMap tm_a, tm_b;  // A [M, K], B [N, K]
+  CUtensorMap tm_gu;       // saved gate/up [M, 2I] (MODE 0: stored, MODE 1: loaded), 32-column boxes
+  CUtensorMap tm_out;      // MODE 0: y [M, I]; MODE 1: dgate/dup [M, 2I]; 32-column boxes
+  int M, n_nt, n_tiles, n_k;
+  uint32_t* status;
+};
+
+// 64B-swizzled [rows][32] 16-bit box: byte offset of 16-byte chunk j of row r.
+__device__ __forceinline__ int box_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using C = GCfg<MODE>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0u, (kKernelId << 16) | 0xFFFFu);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;                     // [NST]
+  uint64_t* empty = bars + C::NST;           // [NST]
+  uint64_t* acc_full = bars + 2 * C::NST;    // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint64_t* fin = acc_full + 4;
+  uint64_t* in_full = fin + 1;               // [E]
+  uint64_t* in_empty = in_full + 4;          // [E]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 29);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_empty[s], 256);
+    }
+    mbar_init(fin, 1);
+    for (int s = 0; s < C::E; ++s) {
+      mbar_init(&in_full[s], 1);
+      mbar_init(&in_empty[s], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx wc{p.status, abort_flag, kKernelId};
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+        const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
+        for (int kc = 0; kc < p.n_k; ++kc, ++it) {
+          const int st = it % C::NST;
+          if (it >= C::NST && !wait_bounded(wc, &empty[st], ((it / C::NST) & 1) ^ 1, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * C::STAGE;
+          mbar_arrive_expect_tx(&full[st], C::STAGE);
+          tma_load_2d(sa, &p.tm_a, &full[st], kc * kBK, mt * kBM);
+          tma_load_2d(sa + C::A_BYTES, &p.tm_b, &full[st], kc * kBK, nt * kBN);
+        }
+      }
+      if (*abort_flag) {
+        for (int j = (it > C::NST ? it - C::NST : 0); j < it; ++j) wait_drain(wc, &full[j % C::NST], (j / C::NST) & 1, 11);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t idesc = make_idesc(kBM, kBN, kBf16, 0, 0);
+      const uint32_t base = smem_u32(smem);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (lt >= 2 && !wait_bounded(wc, &acc_empty[buf], ((lt >> 1) & 1) ^ 1, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * kBN;
+        for (int kc = 0; kc < p.n_k; ++kc, ++it) {
+          const int st = it % C::NST;
+          if (!wait_bounded(wc, &full[st], (it / C::NST) & 1, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = base + st * C::STAGE;
+          const uint32_t b = a + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_ss(d, make_sdesc(a + kk * 32, 16, 1024, kSwizzle128), make_sdesc(b + kk * 32, 16, 1024, kSwizzle128),
+                    idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      umma_commit(fin);
+      wait_drain(wc, fin, 0, 13);
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ epilogue-input loader
+    if constexpr (MODE == 1) {
+      if (lane == 0) {
+        tma_prefetch_desc(&p.tm_gu);
+        int q = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+          const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
+          for (int c = 0; c < kBN / kEC; ++c, ++q) {
+            const int slot = q % C::E;
+            if (q >= C::E && !wait_bounded(wc, &in_empty[slot], ((q / C::E) & 1) ^ 1, 4)) {
+              ok = false;
+              break;
+            }
+            const int col = nt * kBN + c * kEC;            // gate column index in [0, I)
+            const int gcol = (col / kGB) * (2 * kGB) + (col % kGB);
+            uint8_t* dst = smem + C::OFF_IN + slot * 2 * C::BOX;
+            mbar_arrive_expect_tx(&in_full[slot], 2 * C::BOX);
+            tma_load_2d(dst, &p.tm_gu, &in_full[slot], gcol, mt * kBM);
+            tma_load_2d(dst + C::BOX, &p.tm_gu, &in_full[slot], gcol + kGB, mt * kBM);
+          }
+        }
+        if (*abort_flag) {
+          for (int j = (q > C::E ? q - C::E : 0); j < q; ++j) wait_drain(wc, &in_full[j % C::E], (j / C::E) & 1, 12);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int wg = warp >> 2;            // takes the 32-column steps c with c % 2 == wg
+    const int r = threadIdx.x & 127;     // row within the tile = TMEM lane
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    uint8_t* out = smem + C::OFF_OUT + wg * C::N_OUT * C::BOX;
+    bool ok = true;
+    int lt = 0;
+    for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x, ++lt) {
+      const int qt = lt * (kBN / kEC);  // MODE 1: first input-ring step of this tile
+      const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
+      const int buf = lt & 1;
+      if (!__all_sync(0xffffffffu, wait_bounded(wc, &acc_full[buf], (lt >> 1) & 1, 8))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t acc = tmem + lane_off + buf * kBN;
+      if constexpr (MODE == 0) {
+#pragma unroll 1
+        for (int c = wg; c < kGB / kEC; c += 2) {
+          uint32_t zg[32], zu[32];
+          tmem_ld32(acc + c * kEC, zg);
+          tmem_ld32(acc + kGB + c * kEC, zu);
+          tmem_ld_wait();
+          if (c + 2 >= kGB / kEC) {
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+          }
+          uint32_t pg[16], pu[16], py[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            // projections rounded to the activation dtype, as the GEMM output is
+            const float g0 = round_to<T>(__uint_as_float(zg[i])), g1 = round_to<T>(__uint_as_float(zg[i + 1]));
+            const float u0 = round_to<T>(__uint_as_float(zu[i])), u1 = round_to<T>(__uint_as_float(zu[i + 1]));
+            pg[i >> 1] = pack2<T>(g0, g1);
+            pu[i >> 1] = pack2<T>(u0, u1);
+            py[i >> 1] = pack2<T>(round_to<T>(g0 * sigmoid_f32(g0)) * u0, round_to<T>(g1 * sigmoid_f32(g1)) * u1);
+          }
+          // this warpgroup's previous stores must have finished reading its staging boxes
+          if (r == 0) bulk_wait_group_read0();
+          named_bar_sync(1 + wg, 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            *reinterpret_cast<uint4*>(out + box_off(r, j)) = make_uint4(pg[j * 4], pg[j * 4 + 1], pg[j * 4 + 2], pg[j * 4 + 3]);
+            *reinterpret_cast<uint4*>(out + C::BOX + box_off(r, j)) =
+                make_uint4(pu[j * 4], pu[j * 4 + 1], pu[j * 4 + 2], pu[j * 4 + 3]);
+            *reinterpret_cast<uint4*>(out + 2 * C::BOX + box_off(r, j)) =
+                make_uint4(py[j * 4], py[j * 4 + 1], py[j * 4 + 2], py[j * 4 + 3]);
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(1 + wg, 128);
+          if (r == 0) {
+            const int gcol = nt * kBN + c * kEC;  // interleaved gate/up columns of this tile
+            tma_store_2d(&p.tm_gu, out, gcol, mt * kBM);
+            tma_store_2d(&p.tm_gu, out + C::BOX, gcol + kGB, mt * kBM);
+            tma_store_2d(&p.tm_out, out + 2 * C::BOX, nt * kGB + c * kEC, mt * kBM);
+            bulk_commit_group();
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = wg; c < kBN / kEC; c += 2) {
+          const int q = qt + c;  // step index across tiles, in the loader's order
+          uint32_t zd[32];
+          tmem_ld32(acc + c * kEC, zd);
+          tmem_ld_wait();
+          if (c + 2 >= kBN / kEC) {
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+          }
+          const int slot = q % C::E;
+          if (!__all_sync(0xffffffffu, wait_bounded(wc, &in_full[slot], (q / C::E) & 1, 9))) {
+            ok = false;
+            break;
+          }
+          const uint8_t* src = smem + C::OFF_IN + slot * 2 * C::BOX;
+          uint32_t gw[16], uw[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 a = *reinterpret_cast<const uint4*>(src + box_off(r, j));
+            const uint4 b = *reinterpret_cast<const uint4*>(src + C::BOX + box_off(r, j));
+            gw[j * 4] = a.x; gw[j * 4 + 1] = a.y; gw[j * 4 + 2] = a.z; gw[j * 4 + 3] = a.w;
+            uw[j * 4] = b.x; uw[j * 4 + 1] = b.y; uw[j * 4 + 2] = b.z; uw[j * 4 + 3] = b.w;
+          }
+          mbar_arrive(&in_empty[slot]);
+          uint32_t pg[16], pu[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float g[2], u[2], o_g[2], o_u[2];
+            unpack2<T>(gw[i], g[0], g[1]);
+            unpack2<T>(uw[i], u[0], u[1]);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float dy = round_to<T>(__uint_as_float(zd[2 * i + e]));  // dY is a bf16 GEMM output
+              const float s = sigmoid_f32(g[e]);
+              o_g[e] = dy * u[e] * s * (1.f + g[e] * (1.f - s));
+              o_u[e] = dy * round_to<T>(g[e] * s);
+            }
+            pg[i] = pack2<T>(o_g[0], o_g[1]);
+            pu[i] = pack2<T>(o_u[0], o_u[1]);
+          }
+          if (r == 0) bulk_wait_group_read0();
+          named_bar_sync(1 + wg, 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            *reinterpret_cast<uint4*>(out + box_off(r, j)) = make_uint4(pg[j * 4], pg[j * 4 + 1], pg[j * 4 + 2], pg[j * 4 + 3]);
+            *reinterpret_cast<uint4*>(out + C::BOX + box_off(r, j)) =
+                make_uint4(pu[j * 4], pu[j * 4 + 1], pu[j * 4 + 2], pu[j * 4 + 3]);
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(1 + wg, 128);
+          if (r == 0) {
+            const int col = nt * kBN + c * kEC;
+            const int gcol = (col / kGB) * (2 * kGB) + (col % kGB);
+            tma_store_2d(&p.tm_out, out, gcol, mt * kBM);
+            tma_store_2d(&p.tm_out, out + C::BOX, gcol + kGB, mt * kBM);
+            bulk_commit_group();
+          }
+        }
+      }
+    }
+    // stores must finish reading shared memory before the CTA exits
+    if (r == 0) bulk_wait_group0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int map_2d(CUtensorMap* map, int dtype, const void* base, int64_t inner, int64_t outer, int64_t ld, uint32_t box_in,
+           uint32_t box_out, CUtensorMapSwizzle swz) {
+  const CUtensorMapDataType dt = dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  uint64_t dims[2] = {(uint64_t)inner, (uint64_t)outer};
+  uint64_t strides[1] = {(uint64_t)ld * 2};
+  uint32_t box[2] = {box_in, box_out};
+  return encode_tensor_map(map, dt, 2, const_cast<void*>(base), dims, strides, box, swz);
+}
+
+int validate(int dtype, int64_t M, int64_t K, int64_t I, std::initializer_list<const void*> ptrs) {
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (M < 0 || K <= 0 || I <= 0) return MT_ERR_INVALID_ARGUMENT;
+  if (I % kBN != 0 || K % 8 != 0) return MT_ERR_UNSUPPORTED_LAYOUT;  // whole 256-column tiles of gate columns
+  if (M > 0x7fffffffLL - kBM || 2 * I > 0x7fffffffLL) return MT_ERR_INVALID_ARGUMENT;
+  for (const void* q : ptrs)
+    if (M > 0 && (q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) != 0)) return MT_ERR_UNSUPPORTED_LAYOUT;
+  return MT_OK;
+}
+
+template <int MODE>
+int launch(GemmParams& prm, int dtype, int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
+  const int64_t n_mt = (M + kBM - 1) / kBM;
+  prm.M = (int)M;
+  prm.n_nt = (int)(N / kBN);
+  prm.n_tiles = (int)(n_mt * prm.n_nt);
+  prm.n_k = (int)((K + kBK - 1) / kBK);
+  if (n_mt * prm.n_nt > 0x7fffffffLL) return MT_ERR_INVALID_ARGUMENT;
+  const int grid = (int)std::min<int64_t>(prm.n_tiles, get_sm_count());
+  using C = GCfg<MODE>;
+  const bool bf = dtype == MT_BF16;
+  auto kern = bf ? mlp_gemm_kernel<__nv_bfloat16, MODE> : mlp_gemm_kernel<__half, MODE>;
+  int st = set_smem_limit((const void*)kern, C::SMEM);
+  if (st != MT_OK) return st;
+  kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
+  return check_launch(MODE == 0 ? "mlp_gemm_swiglu_fwd" : "mlp_gemm_swiglu_bwd");
+}
+
+}  // namespace
+}  // namespace mt
+
+using namespace mt;
+
+extern "C" int mt_swiglu_gemm_fwd(const void* x, const void* w13, void* gu, void* y, int dtype, int64_t M, int64_t K,
+                                  int64_t I, uint32_t* status, void* stream) {
+  int st = validate(dtype, M, K, I, {x, w13, gu, y});
+  if (st != MT_OK) return st;
+  if (M == 0) return MT_OK;
+  if (status == nullptr) return MT_ERR_INVALID_ARGUMENT;
+  if ((st = bind_device_of(x)) != MT_OK) return st;
+  if ((st = check_arch()) != MT_OK) return st;
+  GemmParams prm;
+  prm.status = status;
+  if ((st = map_2d(&prm.tm_a, dtype, x, K, M, K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w13, K, 2 * I, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_gu, dtype, gu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_out, dtype, y, I, M, I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
+  return launch<0>(prm, dtype, M, K, 2 * I, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mt_swiglu_gemm_bwd(const void* dout, const void* w2t, const void* gu, void* dgu, int dtype, int64_t M,
+                                  int64_t H, int64_t I, uint32_t* status, void* stream) {
+  int st = validate(dtype, M, H, I, {dout, w2t, gu, dgu});
+  if (st != MT_OK) return st;
+  if (M == 0) return MT_OK;
+  if (status == nullptr) return MT_ERR_INVALID_ARGUMENT;
+  if ((st = bind_device_of(dout)) != MT_OK) return st;
+  if ((st = check_arch()) != MT_OK) return st;
+  GemmParams prm;
+  prm.status = status;
+  if ((st = map_2d(&prm.tm_a, dtype, dout, H, M, H, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w2t, H, I, H, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_gu, dtype, gu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_out, dtype, dgu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
+  return launch<1>(prm, dtype, M, H, I, static_cast<cudaStream_t>(stream));
+}

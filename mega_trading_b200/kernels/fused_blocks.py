@@ -13,6 +13,12 @@ Same math as the reference's q/k/v projections + ``RotaryEmbedding`` +
 
 ``swiglu_packed`` is the SwiGLU gate on ``[N, 2I] = [gate | up]`` from one GEMM
 against the concatenated ``[w1; w3]`` weights (``model.py:249-256``).
+
+``swiglu_mlp`` is the whole SwiGLU MLP ``w2(silu(w1 x) * w3 x)`` with the gate
+inside two tcgen05 GEMMs: the gate/up projection writes the saved activation
+and the W2 input in one pass, and the W2 input-gradient GEMM writes the packed
+gate/up gradient directly, so neither the gate output nor its gradient makes
+an extra HBM round trip.
 """
 
 from __future__ import annotations
@@ -116,3 +122,73 @@ def swiglu_packed(gu: torch.Tensor) -> torch.Tensor:
     if gu.shape[-1] % 16 != 0 or not gu.is_contiguous() or gu.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError("gu must be contiguous bf16/fp16 with a last dimension that is a multiple of 16")
     return _SwiGLUPacked.apply(gu)
+
+
+GATE_BLOCK = 128  # interleave block of the fused gate/up weight
+
+
+def interleave_gate_up(w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor:
+    """``[2I, H]`` weight holding w1 and w3 in alternating blocks of 128 rows."""
+    inter, hidden = w1.shape
+    blocks = inter // GATE_BLOCK
+    return torch.stack([w1.reshape(blocks, GATE_BLOCK, hidden), w3.reshape(blocks, GATE_BLOCK, hidden)],
+                       dim=1).reshape(2 * inter, hidden)
+
+
+def swiglu_mlp_supported(inter: int, hidden: int) -> bool:
+    return inter % 256 == 0 and hidden % 8 == 0
+
+
+class _SwiGLUMLP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w13, w2):
+        lib = _lib.load()
+        hidden = x.shape[-1]
+        inter = w13.shape[0] // 2
+        x2 = x.reshape(-1, hidden).contiguous()
+        m = x2.shape[0]
+        gu = torch.empty((m, 2 * inter), device=x.device, dtype=x.dtype)
+        y = torch.empty((m, inter), device=x.device, dtype=x.dtype)
+        status = _lib.status_word(x.device)
+        st = lib.mt_swiglu_gemm_fwd(x2.data_ptr(), w13.data_ptr(), gu.data_ptr(), y.data_ptr(),
+                                    _lib.dtype_code(x.dtype), m, hidden, inter, status.data_ptr(),
+                                    _lib.stream_ptr(x.device))
+        _lib.check(st, "swiglu_gemm forward")
+        _lib.count(1)
+        out = torch.nn.functional.linear(y, w2)
+        ctx.save_for_backward(x2, w13, w2, gu, y)
+        return out.view(*x.shape[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, dout):
+        lib = _lib.load()
+        x2, w13, w2, gu, y = ctx.saved_tensors
+        hidden = x2.shape[1]
+        inter = gu.shape[1] // 2
+        d2 = dout.reshape(-1, w2.shape[0]).contiguous()
+        dw2 = d2.t().mm(y)
+        w2t = w2.t().contiguous()
+        dgu = torch.empty_like(gu)
+        status = _lib.status_word(gu.device)
+        st = lib.mt_swiglu_gemm_bwd(d2.data_ptr(), w2t.data_ptr(), gu.data_ptr(), dgu.data_ptr(),
+                                    _lib.dtype_code(gu.dtype), gu.shape[0], w2.shape[0], inter, status.data_ptr(),
+                                    _lib.stream_ptr(gu.device))
+        _lib.check(st, "swiglu_gemm backward")
+        _lib.count(1)
+        dx = dgu.mm(w13)
+        dw13 = dgu.t().mm(x2)
+        return dx.view(*dout.shape[:-1], hidden), dw13, dw2
+
+
+def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    """``w2(silu(w1 x) * w3 x)`` for ``w13 = interleave_gate_up(w1, w3)`` (16-bit, same dtype as x)."""
+    _lib.require_cuda_sm100(x, "swiglu_mlp")
+    inter, hidden = w13.shape[0] // 2, x.shape[-1]
+    if w13.shape != (2 * inter, hidden) or w2.shape != (hidden, inter):
+        raise ValueError("w13 must be [2I, H] and w2 [H, I]")
+    if not swiglu_mlp_supported(inter, hidden):
+        raise ValueError("swiglu_mlp needs I a multiple of 256 and H a multiple of 8")
+    if x.dtype not in (torch.bfloat16, torch.float16) or w13.dtype != x.dtype or w2.dtype != x.dtype:
+        raise ValueError("x, w13 and w2 must share a 16-bit dtype")
+    return _SwiGLUMLP.apply(x, w13.contiguous(), w2.contiguous())
+

@@ -9,6 +9,8 @@
   4*B*Hq*D*T(T+1)/2 forward; backward 2.5x forward).
 * ce: config 2 -- N=65,536 rows, hidden 768, vocab 21,504; forward
   (2NHV FLOP) and the logit-gradient kernel (2NHV FLOP).
+* mlp: the SwiGLU GEMMs with the gate in the epilogue (2NH*2I forward,
+  2NHI backward) against cuBLAS + the standalone packed gate.
 * rmsnorm / rope / swiglu: config 2 token count, HBM GB/s of the algorithmic
   bytes (each input read once, each output written once).
 
@@ -191,6 +193,50 @@ def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65
     return out
 
 
+def mlp_cases(dev, iters, profile, n=65536, h=768, inter=2048):
+    """SwiGLU MLP: the fused tcgen05 GEMMs against cuBLAS + the standalone packed gate."""
+    import torch.nn.functional as F
+
+    from .kernels.fused_blocks import interleave_gate_up
+
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(n, h, device=dev, generator=g).bfloat16()
+    w1 = torch.randn(inter, h, device=dev, generator=g) * 0.05
+    w3 = torch.randn(inter, h, device=dev, generator=g) * 0.05
+    w13 = interleave_gate_up(w1, w3).bfloat16().contiguous()
+    w13c = torch.cat([w1, w3]).bfloat16()
+    w2t = (torch.randn(inter, h, device=dev, generator=g) * 0.05).bfloat16()
+    dout = torch.randn(n, h, device=dev, generator=g).bfloat16()
+    gu = torch.empty(n, 2 * inter, device=dev, dtype=torch.bfloat16)
+    y = torch.empty(n, inter, device=dev, dtype=torch.bfloat16)
+    dgu = torch.empty_like(gu)
+    status = _lib.status_word(dev)
+    st = _lib.stream_ptr(dev)
+    fwd = lambda: lib.mt_swiglu_gemm_fwd(x.data_ptr(), w13.data_ptr(), gu.data_ptr(), y.data_ptr(), 2, n, h,  # noqa: E731
+                                         inter, status.data_ptr(), st)
+    bwd = lambda: lib.mt_swiglu_gemm_bwd(dout.data_ptr(), w2t.data_ptr(), gu.data_ptr(), dgu.data_ptr(), 2, n,  # noqa: E731
+                                         h, inter, status.data_ptr(), st)
+
+    def unfused_fwd():
+        guc = F.linear(x, w13c)
+        lib.mt_swiglu_packed_fwd(guc.data_ptr(), y.data_ptr(), 2, n, inter, st)
+
+    def unfused_bwd():
+        dy = dout.mm(w2t.t())
+        lib.mt_swiglu_packed_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), 2, n, inter, st)
+
+    if profile:
+        for _ in range(iters):
+            fwd()
+            bwd()
+        return []
+    ff, fb = 2.0 * n * h * 2 * inter, 2.0 * n * h * inter
+    mf, mb, uf, ub = _time(fwd, iters), _time(bwd, iters), _time(unfused_fwd, iters), _time(unfused_bwd, iters)
+    return [{"op": "swiglu_gemm", "N": n, "H": h, "I": inter, "fwd_ms": mf, "fwd_tflops": ff / mf / 1e9,
+             "bwd_ms": mb, "bwd_tflops": fb / mb / 1e9, "unfused_fwd_ms": uf, "unfused_bwd_ms": ub}]
+
+
 def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0, attn_seqs=(1024, 2048, 4096),
         attn_batch: int = 16, ce_rows: int = 65536, heads: int = 16, kv_heads: int = 4) -> list[dict]:
     dev = torch.device("cuda", device)
@@ -200,6 +246,8 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += attention_cases(dev, iters, profile, attn_seqs, attn_batch, heads, kv_heads)
     if "ce" in ops:
         res += ce_cases(dev, iters, profile, n=ce_rows)
+    if "mlp" in ops:
+        res += mlp_cases(dev, iters, profile, n=ce_rows)
     bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))

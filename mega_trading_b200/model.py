@@ -23,7 +23,8 @@ from torch import nn
 
 from .kernels import triton_attention as _attn
 from .kernels import triton_ops as _ops
-from .kernels.fused_blocks import qkv_rope_attention, swiglu_packed
+from .kernels.fused_blocks import (interleave_gate_up, qkv_rope_attention, swiglu_mlp, swiglu_mlp_supported,
+                                   swiglu_packed)
 from .kernels.fused_ce import fused_linear_cross_entropy
 
 
@@ -129,6 +130,11 @@ class SwiGLU(nn.Module):
         self.w3 = nn.Linear(cfg.hidden_dim, cfg.intermediate_dim, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        inter, hidden = self.w1.weight.shape
+        if swiglu_mlp_supported(inter, hidden):
+            # gate inside the projection GEMMs (tcgen05): w1 || w3 interleaved
+            w13 = interleave_gate_up(self.w1.weight, self.w3.weight).to(_BF16)
+            return swiglu_mlp(x, w13, _w(self.w2.weight))
         # one GEMM against [w1; w3]; the gate reads [gate | up] in place
         gu = F.linear(x, torch.cat([self.w1.weight, self.w3.weight], dim=0).to(_BF16))
         return F.linear(swiglu_packed(gu), _w(self.w2.weight))

@@ -80,3 +80,60 @@ def test_fused_blocks_reject_bad_input(cuda_device):
     with pytest.raises(ValueError):
         qkv_rope_attention(torch.zeros(1, 8, 100, device=cuda_device, dtype=torch.bfloat16), cos.to(cuda_device),
                            sin.to(cuda_device), 2, 1, 64)
+
+
+@pytest.mark.parametrize("M,H,I,seed", [(4096, 768, 2048, 61), (300, 256, 512, 62), (1, 768, 256, 63),
+                                        (1000, 64, 768, 64)])
+def test_swiglu_mlp_matches_oracle(cuda_device, M, H, I, seed):
+    """Fused SwiGLU MLP (gate inside the tcgen05 GEMM epilogues) vs the fp32 oracle."""
+    from mega_trading_b200.kernels.fused_blocks import interleave_gate_up, swiglu_mlp
+
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    x = torch.randn(M, H, generator=g)
+    w1 = torch.randn(I, H, generator=g) * 0.05
+    w3 = torch.randn(I, H, generator=g) * 0.05
+    w2 = torch.randn(H, I, generator=g) * 0.05
+    dout = torch.randn(M, H, generator=g)
+    xd, w1d, w3d, w2d = (t.to(cuda_device, bf).requires_grad_(True) for t in (x, w1, w3, w2))
+    out = swiglu_mlp(xd, interleave_gate_up(w1d, w3d), w2d)
+    out.backward(dout.to(cuda_device, bf))
+    xo, w1o, w3o, w2o = (t.to(bf).float().requires_grad_(True) for t in (x, w1, w3, w2))
+    yo = O.swiglu_gate(xo @ w1o.t(), xo @ w3o.t(), act_dtype=bf)
+    oo = yo @ w2o.t()
+    oo.backward(dout.to(bf).float())
+    assert out.shape == (M, H) and out.dtype == bf
+    for name, a, b in (("out", out, oo), ("dx", xd.grad, xo.grad), ("dw1", w1d.grad, w1o.grad),
+                       ("dw3", w3d.grad, w3o.grad), ("dw2", w2d.grad, w2o.grad)):
+        err = O.max_rel_error(a, b)
+        assert err <= TOL, f"{name}: max relative error {err:.3e}"
+
+
+def test_swiglu_gemm_gate_is_bit_exact_with_the_standalone_gate(cuda_device):
+    """The forward epilogue's y equals the standalone packed gate applied to the same saved gate/up."""
+    from mega_trading_b200 import _lib
+    from mega_trading_b200.kernels.fused_blocks import interleave_gate_up
+
+    lib = _lib.load()
+    g = torch.Generator(device=cuda_device).manual_seed(65)
+    M, H, I = 777, 768, 2048
+    x = torch.randn(M, H, device=cuda_device, generator=g).bfloat16()
+    w13 = interleave_gate_up(torch.randn(I, H, device=cuda_device, generator=g) * 0.05,
+                             torch.randn(I, H, device=cuda_device, generator=g) * 0.05).bfloat16().contiguous()
+    gu = torch.empty(M, 2 * I, device=cuda_device, dtype=torch.bfloat16)
+    y = torch.empty(M, I, device=cuda_device, dtype=torch.bfloat16)
+    status = _lib.status_word(cuda_device)
+    _lib.check(lib.mt_swiglu_gemm_fwd(x.data_ptr(), w13.data_ptr(), gu.data_ptr(), y.data_ptr(), 2, M, H, I,
+                                      status.data_ptr(), _lib.stream_ptr(cuda_device)), "swiglu_gemm forward")
+    # the saved activation is the projection rounded to bf16
+    ref = torch.nn.functional.linear(x.float(), w13.float())
+    assert O.max_rel_error(gu, ref) <= 1e-2
+    # [gate | up] from the interleaved layout, then the standalone gate
+    blocks = gu.view(M, I // 128, 2, 128)
+    packed = torch.cat([blocks[:, :, 0].reshape(M, I), blocks[:, :, 1].reshape(M, I)], dim=1).contiguous()
+    y2 = torch.empty_like(y)
+    _lib.check(lib.mt_swiglu_packed_fwd(packed.data_ptr(), y2.data_ptr(), 2, M, I, _lib.stream_ptr(cuda_device)),
+               "swiglu_packed forward")
+    torch.cuda.synchronize()
+    assert _lib.read_status(cuda_device) == 0
+    assert torch.equal(y, y2)
