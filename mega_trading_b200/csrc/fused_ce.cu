@@ -24,8 +24,10 @@
 //     loss; ce_loss_kernel reduces loss and the valid-row count in one block
 //     (fixed order, no host synchronisation).
 //   * dH = dZ W and dW = dZ^T H are plain GEMMs run by the caller.
-// Warp roles (192 threads): warps 0-3 epilogue (thread = row = TMEM lane),
-// warp 4 TMA producer (+ TMEM allocation), warp 5 MMA issuer.
+// Warp roles (320 threads): warps 0-7 epilogue in two warpgroups taking
+// alternate 32-column steps of a tile (thread = row = TMEM lane; MODE 0 merges
+// the two warpgroups' row statistics at the end, MODE 1 gives each warpgroup
+// its own staging box), warp 8 TMA producer (+ TMEM allocation), warp 9 MMA.
 #include <cmath>
 #include <type_traits>
 
@@ -37,18 +39,21 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEC = 32;  // epilogue columns per step
 constexpr uint32_t kKernelId = 3;
 
 template <int MODE>
 struct CeCfg {
-  static constexpr int NST = MODE == 0 ? 4 : 3;
+  static constexpr int NST = 4;
   static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
   static constexpr int B_BYTES = kBN * kBK * 2;  // 32 KB
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int OFF_STAGE = 0;
-  static constexpr int OFF_OUT = NST * STAGE;                          // MODE 1: 4 boxes [128][64] bf16
-  static constexpr int OUT_BYTES = MODE == 1 ? kBM * kBN * 2 : 0;      // 64 KB
+  // MODE 0: [2][128] x {m, s, z} merge area; MODE 1: one [128][32] 16-bit
+  // box (64B swizzle) per epilogue warpgroup
+  static constexpr int OFF_OUT = NST * STAGE;
+  static constexpr int OUT_BYTES = MODE == 1 ? 2 * kBM * kEC * 2 : 3 * kBM * 4;
   static constexpr int OFF_BAR = OFF_OUT + OUT_BYTES;
   static constexpr int SMEM = OFF_BAR + 256;
 };
@@ -108,13 +113,13 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&acc_full[s], 1);
-      mbar_init(&acc_empty[s], 128);
+      mbar_init(&acc_empty[s], 256);
     }
     mbar_init(fin, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -124,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{p.status, abort_flag, kKernelId};
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_h);
       tma_prefetch_desc(&p.tm_w);
@@ -148,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
           wait_drain(wc, &full[j % C::NST], (j / C::NST) & 1, 11);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t idesc = make_idesc(kBM, kBN, kBf16, 0, 0);
@@ -182,14 +187,15 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int r = threadIdx.x;  // 0..127
+    const int wg = warp >> 2;          // takes the 32-column steps c with c % 2 == wg
+    const int r = threadIdx.x & 127;   // row within the tile = TMEM lane
     const int row = row0 + r;
     const bool in_rows = row < p.N;
     const int64_t label = in_rows ? load_label(p, row) : p.ignore_index;
     const bool valid = in_rows && label != p.ignore_index && label >= 0 && label < p.V;
-    if (in_rows && label != p.ignore_index && (label < 0 || label >= p.V))
+    if (wg == 0 && in_rows && label != p.ignore_index && (label < 0 || label >= p.V))
       atomicCAS(p.status, 0u, (kKernelId << 16) | 0xEEEEu);  // out-of-range target
-    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
     float m = -INFINITY, s = 0.f, zy = NAN;
     float lse2 = 0.f, gscale = 0.f;
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
       lse2 = in_rows ? p.lse2[row] : 0.f;
       gscale = valid ? p.scal[2] * p.grad_out[0] : 0.f;
     }
-    uint8_t* out = smem + C::OFF_OUT;
+    uint8_t* out = smem + C::OFF_OUT + wg * (kBM * kEC * 2);
     bool ok = true;
     for (int t = 0; t < n_vt; ++t) {
       const int buf = t & 1;
@@ -207,17 +213,16 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
         break;
       }
       tc_fence_after();
-      if constexpr (MODE == 1) {
-        // staging must be free: the previous tile's TMA stores have read it
-        if (r == 0) bulk_wait_group_read0();
-        named_bar_sync(1, 128);
-      }
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = wg; c < kBN / kEC; c += 2) {
         uint32_t z[32];
-        tmem_ld32(tmem + lane_off + buf * kBN + c * 32, z);
+        tmem_ld32(tmem + lane_off + buf * kBN + c * kEC, z);
         tmem_ld_wait();
-        const int col0 = vbase + c * 32;
+        if (c + 2 >= kBN / kEC) {
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);
+        }
+        const int col0 = vbase + c * kEC;
         if constexpr (MODE == 0) {
           float x[32];
           float cm = -INFINITY;
@@ -239,44 +244,50 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
               if (i == li) zy = __uint_as_float(z[i]);
           }
         } else {
-          float g[32];
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float pr = fast_exp2(__uint_as_float(z[i]) * kLog2e - lse2);
-            g[i] = (pr - ((col0 + i) == label ? 1.f : 0.f)) * gscale;
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = fast_exp2(__uint_as_float(z[i]) * kLog2e - lse2);
+            const float p1 = fast_exp2(__uint_as_float(z[i + 1]) * kLog2e - lse2);
+            pk[i >> 1] = pack2<T>((p0 - ((col0 + i) == label ? 1.f : 0.f)) * gscale,
+                                  (p1 - ((col0 + i + 1) == label ? 1.f : 0.f)) * gscale);
           }
-          // 32 columns = half of a 64-column box: 4 swizzled 16-byte chunks
-          uint8_t* box = out + (c >> 1) * (kBM * 128) + r * 128;
+          // this warpgroup's previous store must have finished reading its box
+          if (r == 0) bulk_wait_group_read0();
+          named_bar_sync(1 + wg, 128);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = (c & 1) * 4 + q;
-            uint4 w;
-            w.x = pack2<T>(g[q * 8 + 0], g[q * 8 + 1]);
-            w.y = pack2<T>(g[q * 8 + 2], g[q * 8 + 3]);
-            w.z = pack2<T>(g[q * 8 + 4], g[q * 8 + 5]);
-            w.w = pack2<T>(g[q * 8 + 6], g[q * 8 + 7]);
-            *reinterpret_cast<uint4*>(box + ((ch ^ (r & 7)) * 16)) = w;
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(out + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) =
+                make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(1 + wg, 128);
+          if (r == 0) {
+            tma_store_2d(&p.tm_dz, out, col0, row0);
+            bulk_commit_group();
           }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
-      if constexpr (MODE == 1) {
-        fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (r == 0) {
-#pragma unroll
-          for (int bx = 0; bx < kBN / 64; ++bx) tma_store_2d(&p.tm_dz, out + bx * (kBM * 128), vbase + bx * 64, row0);
-          bulk_commit_group();
         }
       }
     }
     if constexpr (MODE == 0) {
-      if (ok && in_rows) {
-        const int64_t idx = int64_t(row) * p.splits + split;
-        p.part_m[idx] = m;
-        p.part_s[idx] = s;
-        p.part_z[idx] = zy;
+      // merge the two warpgroups' running statistics of each row
+      float* mg = reinterpret_cast<float*>(smem + C::OFF_OUT);
+      if (wg == 1) {
+        mg[r] = m;
+        mg[128 + r] = s;
+        mg[256 + r] = zy;
+      }
+      named_bar_sync(3, 256);
+      if (wg == 0) {
+        const float m1 = mg[r], s1 = mg[128 + r], z1 = mg[256 + r];
+        const float mn = fmaxf(m, m1);
+        const float sm = (m == -INFINITY ? 0.f : s * fast_exp2(m - mn)) + (m1 == -INFINITY ? 0.f : s1 * fast_exp2(m1 - mn));
+        const float zm = isnan(zy) ? z1 : zy;
+        if (ok && in_rows) {
+          const int64_t idx = int64_t(row) * p.splits + split;
+          p.part_m[idx] = mn;
+          p.part_s[idx] = sm;
+          p.part_z[idx] = zm;
+        }
       }
     } else {
       if (r == 0) bulk_wait_group0();
@@ -285,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -504,8 +515,8 @@ extern "C" int mt_fused_ce_grad_logits(const void* hidden, const void* weight, c
         dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     uint64_t dims[2] = {(uint64_t)V, (uint64_t)N};
     uint64_t str[1] = {(uint64_t)dz_ld * 2};
-    uint32_t box[2] = {64, kBM};
-    if ((st = encode_tensor_map(&prm.tm_dz, dt, 2, dz, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK)
+    uint32_t box[2] = {kEC, kBM};
+    if ((st = encode_tensor_map(&prm.tm_dz, dt, 2, dz, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK)
       return st;
   }
   prm.labels = labels;
