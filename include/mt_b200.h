@@ -259,6 +259,24 @@ MT_API int mt_swiglu_gemm_bwd(const void* dout, const void* w2t, const void* gu,
                        uint32_t* status, void* stream);
 
 /* ---------------------------------------------------------------------
+ * QKV projection + RoPE   replaces the q/k/v projections and
+ *   RotaryEmbedding / triton_apply_rope forward of LlamaAttention
+ *   (src/mega_trading/model.py:218-226, 286-294; kernels/triton_ops.py:45-54).
+ *   tcgen05 GEMM qkv = round(x w^T) whose epilogue rotates the first
+ *   rot_cols columns (the q and k heads) of each row by the RoPE tables at
+ *   position t = row % seq: interleaved pairs (e c - o s, e s + o c), tables
+ *   rope_cos / rope_sin [seq, head_dim/2] in dtype with row stride rope_ld
+ *   (a multiple of 8).  x [M, K], w [N, K], qkv [M, N] row-major; M a
+ *   multiple of seq, N a multiple of 256, head_dim 32 or 64, rot_cols a
+ *   multiple of head_dim.  No counterpart kernel in the reference.
+ * ------------------------------------------------------------------- */
+MT_API int mt_qkv_rope_gemm(const void* x, const void* w, void* qkv,
+                     const void* rope_cos, const void* rope_sin, int64_t rope_ld,
+                     int dtype, int64_t M, int64_t K, int64_t N, int64_t rot_cols,
+                     int64_t seq, int64_t head_dim, uint32_t* status,
+                     void* stream);
+
+/* ---------------------------------------------------------------------
  * Fused linear + cross-entropy   replaces triton_fused_linear_cross_entropy
  *   (src/mega_trading/kernels/triton_ops.py:64-92, :294-411, row kernel
  *    :822-887; torch path :99-112)

@@ -56,6 +56,8 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     ),
     "mt_swiglu_gemm_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "mt_swiglu_gemm_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "mt_qkv_rope_gemm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                 c_vp, c_vp]),
     "mt_rope": (
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p,

@@ -26,6 +26,11 @@
 //     boxes of the saved activation through a 3-slot ring; the epilogue rounds
 //     dY to bf16 (the GEMM output dtype) and writes dgate / dup in the
 //     interleaved layout: dg = dy u s (1 + g (1 - s)), du = dy round(g s).
+//   MODE 2 (QKV projection + RoPE): B = [Wq; Wk; Wv]; the epilogue rounds the
+//     projection to bf16 and rotates the q and k columns (the first rot_cols)
+//     of the token at position t = row % T by the 16-bit RoPE tables
+//     (interleaved pairs: (e c - o s, e s + o c), model.py:286-316), writing
+//     the packed [q_rot | k_rot | v] rows attention reads in place.
 // Warp roles (352 threads): warps 0-7 epilogue in two warpgroups taking
 // alternate 32-column steps (each with its own staging boxes), 8 TMA producer
 // (+ TMEM allocation), 9 MMA issuer, 10 epilogue-input loader (MODE 1).
@@ -49,13 +54,13 @@ constexpr uint32_t kKernelId = 6;
 
 template <int MODE>
 struct GCfg {
-  static constexpr int NST = 3;
+  static constexpr int NST = MODE == 2 ? 4 : 3;
   static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
   static constexpr int B_BYTES = kBN * kBK * 2;  // 32 KB
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BOX = kBM * kEC * 2;      // [128 rows][32 cols] 16-bit = 8 KB, 64 B rows
-  static constexpr int N_OUT = MODE == 0 ? 3 : 2;
-  static constexpr int E = MODE == 0 ? 0 : 3;    // epilogue-input ring slots (gate + up box each)
+  static constexpr int N_OUT = MODE == 0 ? 3 : (MODE == 1 ? 2 : 1);
+  static constexpr int E = MODE == 1 ? 3 : 0;    // epilogue-input ring slots (gate + up box each)
   static constexpr int OFF_OUT = NST * STAGE;    // [2 warpgroups][N_OUT boxes]
   static constexpr int OFF_IN = OFF_OUT + 2 * N_OUT * BOX;
   static constexpr int OFF_BAR = OFF_IN + E * 2 * BOX;
@@ -68,6 +73,11 @@ struct GemmParams {
   CUtensorMap tm_gu;       // saved gate/up [M, 2I] (MODE 0: stored, MODE 1: loaded), 32-column boxes
   CUtensorMap tm_out;      // MODE 0: y [M, I]; MODE 1: dgate/dup [M, 2I]; 32-column boxes
   int M, n_nt, n_tiles, n_k;
+  // MODE 2: RoPE tables [T, head_dim / 2] (row stride rope_ld) and geometry
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_ld;
+  int seq, head_dim, rot_cols;
   uint32_t* status;
 };
 
@@ -268,6 +278,60 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
             bulk_commit_group();
           }
         }
+      } else if constexpr (MODE == 2) {
+        const int row = mt * kBM + r;
+        const int t_pos = row % p.seq;
+#pragma unroll 1
+        for (int c = wg; c < kBN / kEC; c += 2) {
+          uint32_t z[32];
+          tmem_ld32(acc + c * kEC, z);
+          tmem_ld_wait();
+          if (c + 2 >= kBN / kEC) {
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+          }
+          const int col0 = nt * kBN + c * kEC;
+          uint32_t pk[16];
+          if (col0 < p.rot_cols) {
+            // pairs (2i, 2i+1) of this head: table entries i0 .. i0 + 15
+            const int i0 = (col0 % p.head_dim) >> 1;
+            const T* cp = static_cast<const T*>(p.rope_cos) + int64_t(t_pos) * p.rope_ld + i0;
+            const T* sp = static_cast<const T*>(p.rope_sin) + int64_t(t_pos) * p.rope_ld + i0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint4 cr = *reinterpret_cast<const uint4*>(cp + h * 8);
+              const uint4 sr = *reinterpret_cast<const uint4*>(sp + h * 8);
+              const uint32_t cw[4] = {cr.x, cr.y, cr.z, cr.w}, sw[4] = {sr.x, sr.y, sr.z, sr.w};
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                float cs[2], sn[2];
+                unpack2<T>(cw[w], cs[0], cs[1]);
+                unpack2<T>(sw[w], sn[0], sn[1]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int i = h * 8 + w * 2 + e;  // pair index within the chunk
+                  const float ev = round_to<T>(__uint_as_float(z[2 * i]));
+                  const float od = round_to<T>(__uint_as_float(z[2 * i + 1]));
+                  pk[i] = pack2<T>(ev * cs[e] - od * sn[e], ev * sn[e] + od * cs[e]);
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = pack2<T>(__uint_as_float(z[2 * i]), __uint_as_float(z[2 * i + 1]));
+          }
+          if (r == 0) bulk_wait_group_read0();
+          named_bar_sync(1 + wg, 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(out + box_off(r, j)) = make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(1 + wg, 128);
+          if (r == 0) {
+            tma_store_2d(&p.tm_out, out, col0, mt * kBM);
+            bulk_commit_group();
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = wg; c < kBN / kEC; c += 2) {
@@ -376,7 +440,7 @@ int launch(GemmParams& prm, int dtype, int64_t M, int64_t K, int64_t N, cudaStre
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
   kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
-  return check_launch(MODE == 0 ? "mlp_gemm_swiglu_fwd" : "mlp_gemm_swiglu_bwd");
+  return check_launch(MODE == 0 ? "mlp_gemm_swiglu_fwd" : (MODE == 1 ? "mlp_gemm_swiglu_bwd" : "qkv_gemm_rope"));
 }
 
 }  // namespace
@@ -417,3 +481,35 @@ extern "C" int mt_swiglu_gemm_bwd(const void* dout, const void* w2t, const void*
   if ((st = map_2d(&prm.tm_out, dtype, dgu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   return launch<1>(prm, dtype, M, H, I, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" int mt_qkv_rope_gemm(const void* x, const void* w, void* qkv, const void* rope_cos, const void* rope_sin,
+                                int64_t rope_ld, int dtype, int64_t M, int64_t K, int64_t N, int64_t rot_cols,
+                                int64_t seq, int64_t head_dim, uint32_t* status, void* stream) {
+  if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
+  if (M < 0 || K <= 0 || N <= 0 || seq <= 0 || rot_cols < 0 || rot_cols > N) return MT_ERR_INVALID_ARGUMENT;
+  if (M > 0 && M % seq != 0) return MT_ERR_INVALID_ARGUMENT;  // whole sequences of seq tokens
+  if (N % kBN != 0 || K % 8 != 0 || (head_dim != 32 && head_dim != 64) || rot_cols % head_dim != 0)
+    return MT_ERR_UNSUPPORTED_LAYOUT;
+  if (M > 0x7fffffffLL - kBM || N > 0x7fffffffLL) return MT_ERR_INVALID_ARGUMENT;
+  if (M == 0) return MT_OK;
+  if (status == nullptr || rope_cos == nullptr || rope_sin == nullptr || rope_ld < head_dim / 2) return MT_ERR_INVALID_ARGUMENT;
+  for (const void* q : {x, w, static_cast<const void*>(qkv), rope_cos, rope_sin})
+    if (q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) != 0) return MT_ERR_UNSUPPORTED_LAYOUT;
+  if (rope_ld % 8 != 0) return MT_ERR_UNSUPPORTED_LAYOUT;  // 16-byte table rows (8 pairs per load)
+  int st = bind_device_of(x);
+  if (st != MT_OK) return st;
+  if ((st = check_arch()) != MT_OK) return st;
+  GemmParams prm;
+  prm.status = status;
+  prm.rope_cos = rope_cos;
+  prm.rope_sin = rope_sin;
+  prm.rope_ld = rope_ld;
+  prm.seq = (int)seq;
+  prm.head_dim = (int)head_dim;
+  prm.rot_cols = (int)rot_cols;
+  if ((st = map_2d(&prm.tm_a, dtype, x, K, M, K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w, K, N, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_out, dtype, qkv, N, M, N, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
+  return launch<2>(prm, dtype, M, K, N, static_cast<cudaStream_t>(stream));
+}
+

@@ -10,6 +10,9 @@ the projection is again ONE GEMM and no gradient slices are copied or added;
 the RoPE backward is folded into the attention backward's dq / dk epilogues.
 Same math as the reference's q/k/v projections + ``RotaryEmbedding`` +
 ``triton_attention`` (``src/mega_trading/model.py:218-237, 286-294``).
+``qkv_proj_rope_attention`` also owns the projection: a tcgen05 GEMM whose
+epilogue applies RoPE, so the rotated q/k are written once, straight from the
+accumulator.
 
 ``swiglu_packed`` is the SwiGLU gate on ``[N, 2I] = [gate | up]`` from one GEMM
 against the concatenated ``[w1; w3]`` weights (``model.py:249-256``).
@@ -85,6 +88,68 @@ def qkv_rope_attention(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, 
     cos2 = _ops._table_2d(cos, T, head_dim // 2, qkv.dtype)
     sin2 = _ops._table_2d(sin, T, head_dim // 2, qkv.dtype)
     return _QKVRopeAttention.apply(qkv, cos2, sin2, heads, kv_heads, head_dim)
+
+
+def qkv_rope_gemm_supported(heads: int, kv_heads: int, head_dim: int, hidden: int) -> bool:
+    return (heads + 2 * kv_heads) * head_dim % 256 == 0 and head_dim in (32, 64) and hidden % 8 == 0
+
+
+def _qkv_rope_gemm(x2, w, cos2, sin2, seq, rot_cols, head_dim):
+    lib = _lib.load()
+    m, hidden = x2.shape
+    n = w.shape[0]
+    qkv = torch.empty((m, n), device=x2.device, dtype=x2.dtype)
+    status = _lib.status_word(x2.device)
+    st = lib.mt_qkv_rope_gemm(x2.data_ptr(), w.data_ptr(), qkv.data_ptr(), cos2.data_ptr(), sin2.data_ptr(),
+                              cos2.stride(0), _lib.dtype_code(x2.dtype), m, hidden, n, rot_cols, seq, head_dim,
+                              status.data_ptr(), _lib.stream_ptr(x2.device))
+    _lib.check(st, "qkv_rope_gemm")
+    _lib.count(1)
+    return qkv
+
+
+class _QKVProjRopeAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, cos2, sin2, hq, hkv, d):
+        B, T, H = x.shape
+        x2 = x.reshape(B * T, H).contiguous()
+        qkv = _qkv_rope_gemm(x2, w, cos2, sin2, T, (hq + hkv) * d, d).view(B, T, -1)
+        q_rot, k_rot, v = _split(qkv, hq, hkv, d)
+        scale = 1.0 / math.sqrt(d)
+        o, lse = _attn._launch_fwd(q_rot, k_rot, v, hq // hkv, scale)
+        ctx.save_for_backward(x2, w, q_rot, k_rot, v, o, lse, cos2, sin2)
+        ctx.dims = (hq, hkv, d)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_o):
+        x2, w, q_rot, k_rot, v, o, lse, cos2, sin2 = ctx.saved_tensors
+        hq, hkv, d = ctx.dims
+        B, _, T, _ = q_rot.shape
+        do = _attn._aligned_view(grad_o)
+        n = (hq + 2 * hkv) * d
+        dqkv = torch.empty((B, T, n), device=q_rot.device, dtype=q_rot.dtype)
+        dq, dk, dv = _split(dqkv, hq, hkv, d)
+        _attn._launch_bwd(q_rot, k_rot, v, o, lse, do, ctx.scale, dq=dq, dk=dk, dv=dv, rope=(cos2, sin2))
+        d2 = dqkv.view(B * T, n)
+        return d2.mm(w).view(B, T, -1), d2.t().mm(x2), None, None, None, None, None
+
+
+def qkv_proj_rope_attention(x: torch.Tensor, w_qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, heads: int,
+                            kv_heads: int, head_dim: int) -> torch.Tensor:
+    """Causal GQA attention of ``x`` projected by ``w_qkv = [Wq; Wk; Wv]`` with RoPE in the GEMM epilogue."""
+    _lib.require_cuda_sm100(x, "qkv_proj_rope_attention")
+    if x.dim() != 3 or w_qkv.shape != ((heads + 2 * kv_heads) * head_dim, x.shape[-1]):
+        raise ValueError("x must be [batch, time, hidden] and w_qkv [(heads + 2 * kv_heads) * head_dim, hidden]")
+    if not qkv_rope_gemm_supported(heads, kv_heads, head_dim, x.shape[-1]):
+        raise ValueError("qkv_proj_rope_attention needs (heads + 2 kv_heads) head_dim a multiple of 256")
+    if x.dtype not in (torch.bfloat16, torch.float16) or w_qkv.dtype != x.dtype:
+        raise ValueError("x and w_qkv must share a 16-bit dtype")
+    T = x.shape[1]
+    cos2 = _ops._table_2d(cos, T, head_dim // 2, x.dtype).contiguous()
+    sin2 = _ops._table_2d(sin, T, head_dim // 2, x.dtype).contiguous()
+    return _QKVProjRopeAttention.apply(x, w_qkv.contiguous(), cos2, sin2, heads, kv_heads, head_dim)
 
 
 class _SwiGLUPacked(torch.autograd.Function):

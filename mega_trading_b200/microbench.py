@@ -237,6 +237,45 @@ def mlp_cases(dev, iters, profile, n=65536, h=768, inter=2048):
              "bwd_ms": mb, "bwd_tflops": fb / mb / 1e9, "unfused_fwd_ms": uf, "unfused_bwd_ms": ub}]
 
 
+def qkv_cases(dev, iters, profile, n=65536, h=768, hq=12, hkv=4, d=64, seq=2048):
+    """QKV projection with RoPE in the tcgen05 epilogue against cuBLAS + the RoPE kernel."""
+    import torch.nn.functional as F
+
+    from .kernels import triton_ops as K
+
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(13)
+    cols = (hq + 2 * hkv) * d
+    x = torch.randn(n, h, device=dev, generator=g).bfloat16()
+    w = (torch.randn(cols, h, device=dev, generator=g) * 0.04).bfloat16()
+    pos = torch.arange(seq, device=dev, dtype=torch.float32)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, d, 2, device=dev, dtype=torch.float32) / d))
+    fr = torch.outer(pos, inv)
+    cos2, sin2 = fr.cos().bfloat16().contiguous(), fr.sin().bfloat16().contiguous()
+    qkv = torch.empty(n, cols, device=dev, dtype=torch.bfloat16)
+    status = _lib.status_word(dev)
+    st = _lib.stream_ptr(dev)
+    fused = lambda: lib.mt_qkv_rope_gemm(x.data_ptr(), w.data_ptr(), qkv.data_ptr(), cos2.data_ptr(),  # noqa: E731
+                                         sin2.data_ptr(), d // 2, 2, n, h, cols, (hq + hkv) * d, seq, d,
+                                         status.data_ptr(), st)
+    B = n // seq
+
+    def unfused():
+        y = F.linear(x, w).view(B, seq, cols)
+        q = y[..., : hq * d].view(B, seq, hq, d).transpose(1, 2)
+        k = y[..., hq * d:(hq + hkv) * d].view(B, seq, hkv, d).transpose(1, 2)
+        K._launch_rope(q, k, cos2, sin2, torch.empty_like(q), torch.empty_like(k), negate=False)
+
+    if profile:
+        for _ in range(iters):
+            fused()
+        return []
+    fl = 2.0 * n * h * cols
+    mf, mu = _time(fused, iters), _time(unfused, iters)
+    return [{"op": "qkv_rope_gemm", "N": n, "H": h, "cols": cols, "ms": mf, "tflops": fl / mf / 1e9,
+             "unfused_ms": mu}]
+
+
 def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0, attn_seqs=(1024, 2048, 4096),
         attn_batch: int = 16, ce_rows: int = 65536, heads: int = 16, kv_heads: int = 4) -> list[dict]:
     dev = torch.device("cuda", device)
@@ -248,6 +287,8 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += ce_cases(dev, iters, profile, n=ce_rows)
     if "mlp" in ops:
         res += mlp_cases(dev, iters, profile, n=ce_rows)
+    if "qkv" in ops:
+        res += qkv_cases(dev, iters, profile, n=ce_rows)
     bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))

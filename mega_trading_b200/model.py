@@ -23,8 +23,8 @@ from torch import nn
 
 from .kernels import triton_attention as _attn
 from .kernels import triton_ops as _ops
-from .kernels.fused_blocks import (interleave_gate_up, qkv_rope_attention, swiglu_mlp, swiglu_mlp_supported,
-                                   swiglu_packed)
+from .kernels.fused_blocks import (interleave_gate_up, qkv_proj_rope_attention, qkv_rope_attention,
+                                   qkv_rope_gemm_supported, swiglu_mlp, swiglu_mlp_supported, swiglu_packed)
 from .kernels.fused_ce import fused_linear_cross_entropy
 
 
@@ -106,8 +106,12 @@ class LlamaAttention(nn.Module):
         # one projection GEMM against [q_proj; k_proj; v_proj]; RoPE + attention
         # read the packed output in place and write one packed gradient
         w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], dim=0).to(_BF16)
-        qkv = F.linear(x, w_qkv)
-        o = qkv_rope_attention(qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
+        if qkv_rope_gemm_supported(self.heads, self.kv_heads, self.head_dim, H):
+            # RoPE in the projection GEMM's epilogue (tcgen05)
+            o = qkv_proj_rope_attention(x, w_qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
+        else:
+            qkv = F.linear(x, w_qkv)
+            o = qkv_rope_attention(qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
         # o is stored [B, T, H, D]: the transpose is free
         return F.linear(o.transpose(1, 2).reshape(B, T, H), _w(self.o_proj.weight))
 

@@ -137,3 +137,70 @@ def test_swiglu_gemm_gate_is_bit_exact_with_the_standalone_gate(cuda_device):
     torch.cuda.synchronize()
     assert _lib.read_status(cuda_device) == 0
     assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("B,T,H,Hq,Hkv,D,theta,seed", [(2, 256, 768, 12, 4, 64, 500_000.0, 71),
+                                                       (1, 300, 256, 8, 4, 32, 10_000.0, 72),
+                                                       (3, 128, 512, 4, 2, 64, 10_000.0, 73)])
+def test_qkv_proj_rope_attention_matches_oracle(cuda_device, B, T, H, Hq, Hkv, D, theta, seed):
+    """Projection GEMM with RoPE in its epilogue + attention, vs the fp32 oracle chain."""
+    from mega_trading_b200.kernels.fused_blocks import qkv_proj_rope_attention
+
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    n = (Hq + 2 * Hkv) * D
+    x = torch.randn(B, T, H, generator=g)
+    w = torch.randn(n, H, generator=g) * (1.0 / H ** 0.5)
+    do = torch.randn(B, T, Hq, D, generator=g)
+    cos, sin = O.rope_tables(D, T, theta)
+    xd, wd = x.to(cuda_device, bf).requires_grad_(True), w.to(cuda_device, bf).requires_grad_(True)
+    o = qkv_proj_rope_attention(xd, wd, cos.to(cuda_device), sin.to(cuda_device), Hq, Hkv, D)
+    assert o.shape == (B, Hq, T, D) and o.transpose(1, 2).is_contiguous()
+    o.backward(do.to(cuda_device, bf).transpose(1, 2))
+    xo, wo = x.to(bf).float().requires_grad_(True), w.to(bf).float().requires_grad_(True)
+    qkv = xo @ wo.t()
+    q = qkv[..., : Hq * D].reshape(B, T, Hq, D).transpose(1, 2)
+    k = qkv[..., Hq * D:(Hq + Hkv) * D].reshape(B, T, Hkv, D).transpose(1, 2)
+    v = qkv[..., (Hq + Hkv) * D:].reshape(B, T, Hkv, D).transpose(1, 2)
+    rq, rk = O.apply_rope(q, k, cos, sin, table_dtype=bf)
+    oo = O.causal_gqa_attention(rq, rk, v, Hq // Hkv)
+    oo.backward(do.to(bf).float().transpose(1, 2))
+    for name, a, b in (("o", o, oo), ("dx", xd.grad, xo.grad), ("dw", wd.grad, wo.grad)):
+        err = O.max_rel_error(a, b)
+        assert err <= TOL, f"{name}: max relative error {err:.3e}"
+
+
+def test_qkv_rope_gemm_rotation_is_bit_exact_with_the_rope_kernel(cuda_device):
+    """Epilogue RoPE == the standalone RoPE kernel applied to the same rounded projection."""
+    from mega_trading_b200 import _lib
+    from mega_trading_b200.kernels import triton_ops as K
+
+    lib = _lib.load()
+    g = torch.Generator(device=cuda_device).manual_seed(74)
+    B, T, H, Hq, Hkv, D = 2, 384, 768, 12, 4, 64
+    n = (Hq + 2 * Hkv) * D
+    x = torch.randn(B * T, H, device=cuda_device, generator=g).bfloat16()
+    w = (torch.randn(n, H, device=cuda_device, generator=g) * 0.04).bfloat16()
+    cos, sin = O.rope_tables(D, T, 500_000.0)
+    cos2 = cos.reshape(T, D // 2).to(cuda_device, torch.bfloat16).contiguous()
+    sin2 = sin.reshape(T, D // 2).to(cuda_device, torch.bfloat16).contiguous()
+    status = _lib.status_word(cuda_device)
+    outs = []
+    for rot in ((Hq + Hkv) * D, 0):
+        qkv = torch.empty(B * T, n, device=cuda_device, dtype=torch.bfloat16)
+        _lib.check(lib.mt_qkv_rope_gemm(x.data_ptr(), w.data_ptr(), qkv.data_ptr(), cos2.data_ptr(), sin2.data_ptr(),
+                                        D // 2, 2, B * T, H, n, rot, T, D, status.data_ptr(),
+                                        _lib.stream_ptr(cuda_device)), "qkv_rope_gemm")
+        outs.append(qkv.view(B, T, n))
+    fused, plain = outs
+    q = plain[..., : Hq * D].view(B, T, Hq, D).transpose(1, 2)
+    k = plain[..., Hq * D:(Hq + Hkv) * D].view(B, T, Hkv, D).transpose(1, 2)
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    K._launch_rope(q, k, cos2, sin2, qo, ko, negate=False)
+    torch.cuda.synchronize()
+    assert _lib.read_status(cuda_device) == 0
+    assert torch.equal(fused[..., : Hq * D].view(B, T, Hq, D), qo.transpose(1, 2))
+    assert torch.equal(fused[..., Hq * D:(Hq + Hkv) * D].view(B, T, Hkv, D), ko.transpose(1, 2))
+    assert torch.equal(fused[..., (Hq + Hkv) * D:], plain[..., (Hq + Hkv) * D:])
+    ref = torch.nn.functional.linear(x.float(), w.float()).view(B, T, n)
+    assert O.max_rel_error(plain, ref) <= 1e-2
