@@ -9,6 +9,8 @@
   4*B*Hq*D*T(T+1)/2 forward; backward 2.5x forward).
 * ce: config 2 -- N=65,536 rows, hidden 768, vocab 21,504; forward
   (2NHV FLOP) and the logit-gradient kernel (2NHV FLOP).
+* torch: the BASELINE torch comparators on the same box (SDPA flash/cuDNN,
+  F.rms_norm, eager RoPE, F.silu * up, F.linear + F.cross_entropy).
 * mlp: the SwiGLU GEMMs with the gate in the epilogue (2NH*2I forward,
   2NHI backward) against cuBLAS + the standalone packed gate.
 * rmsnorm / rope / swiglu: config 2 token count, HBM GB/s of the algorithmic
@@ -276,6 +278,63 @@ def qkv_cases(dev, iters, profile, n=65536, h=768, hq=12, hkv=4, d=64, seq=2048)
              "unfused_ms": mu}]
 
 
+def torch_comparators(dev, iters, seqs=(1024, 2048, 4096), n=65536):
+    """The BASELINE torch comparators on the same box: SDPA (flash / cuDNN backends) for causal
+    GQA attention at config 1, F.rms_norm, eager RoPE, F.silu * up and F.linear + F.cross_entropy
+    at config 2 (library kernels, timed like ours)."""
+    import torch.nn.functional as F
+
+    out = []
+    for T in seqs:
+        B, Hq, Hkv, D = 16, 16, 4, 64
+        g = torch.Generator(device=dev).manual_seed(T)
+        q = (torch.randn(B, Hq, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        k = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        v = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        do = torch.randn(B, Hq, T, D, device=dev, generator=g).bfloat16()
+        fwd = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)  # noqa: E731
+        o = fwd()
+        bwd = lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)  # noqa: E731
+        flops = 4.0 * B * Hq * D * T * (T + 1) / 2
+        mf, mb = _time(fwd, iters), _time(bwd, iters)
+        out.append({"op": "torch_sdpa", "T": T, "B": B, "fwd_ms": mf, "fwd_tflops": flops / mf / 1e9, "bwd_ms": mb,
+                    "bwd_tflops": 2.5 * flops / mb / 1e9, "fwd_bwd_tflops": 3.5 * flops / (mf + mb) / 1e9})
+        del q, k, v, do, o
+    g = torch.Generator(device=dev).manual_seed(9)
+    H, I, V = 768, 2048, 21504
+    x = torch.randn(n, H, device=dev, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).bfloat16()
+    mf = _time(lambda: F.rms_norm(x, (H,), w, eps=1e-5), iters)
+    out.append({"op": "torch_rms_norm", "N": n, "H": H, "fwd_ms": mf, "fwd_gbs": (2 * n * H * 2 + 4 * n) / mf / 1e6})
+    gt = torch.randn(n, I, device=dev, generator=g).bfloat16()
+    up = torch.randn(n, I, device=dev, generator=g).bfloat16()
+    mf = _time(lambda: F.silu(gt) * up, iters)
+    out.append({"op": "torch_swiglu", "N": n, "I": I, "fwd_ms": mf, "fwd_gbs": 3 * n * I * 2 / mf / 1e6})
+    del gt, up
+    Bt, T, D = n // 2048, 2048, 64
+    qr = torch.randn(Bt, 12, T, D, device=dev, generator=g).bfloat16()
+    kr = torch.randn(Bt, 4, T, D, device=dev, generator=g).bfloat16()
+    fr = torch.outer(torch.arange(T, device=dev, dtype=torch.float32),
+                     1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)))
+    c, sn = fr.cos().bfloat16(), fr.sin().bfloat16()
+
+    def rot(t):
+        e, o2 = t[..., 0::2], t[..., 1::2]
+        return torch.stack((e * c - o2 * sn, e * sn + o2 * c), dim=-1).flatten(-2)
+
+    mf = _time(lambda: (rot(qr), rot(kr)), iters)
+    out.append({"op": "torch_rope", "N": n, "ms": mf, "gbs": 2 * n * 16 * D * 2 / mf / 1e6})
+    del qr, kr
+    hid = (torch.randn(n, H, device=dev, generator=g) * 0.5).bfloat16()
+    wv = (torch.randn(V, H, device=dev, generator=g) * 0.02).bfloat16()
+    lab = torch.randint(0, V, (n,), device=dev, generator=g)
+    ce = lambda: F.cross_entropy(F.linear(hid, wv).float(), lab)  # noqa: E731
+    mf = _time(ce, max(2, iters // 2))
+    out.append({"op": "torch_linear_ce", "N": n, "H": H, "V": V, "fwd_ms": mf,
+                "fwd_tflops": 2.0 * n * H * V / mf / 1e9})
+    return out
+
+
 def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0, attn_seqs=(1024, 2048, 4096),
         attn_batch: int = 16, ce_rows: int = 65536, heads: int = 16, kv_heads: int = 4) -> list[dict]:
     dev = torch.device("cuda", device)
@@ -289,6 +348,8 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += mlp_cases(dev, iters, profile, n=ce_rows)
     if "qkv" in ops:
         res += qkv_cases(dev, iters, profile, n=ce_rows)
+    if "torch" in ops and not profile:
+        res += torch_comparators(dev, iters, attn_seqs)
     bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))
