@@ -158,6 +158,26 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Rounding to the 16-bit activation type on the integer pipe, for epilogues
+// whose conversion instructions would otherwise saturate the XU pipe next to
+// the exponentials.  bf16: round-to-nearest-even on the bit pattern, the same
+// result as cvt.rn.bf16.f32 for every finite value and for +-inf (NaN stays
+// NaN except for payloads at the top of the range).  fp16 keeps the
+// conversion instruction.
+template <typename T> __device__ __forceinline__ float round_epi(float v);
+template <> __device__ __forceinline__ float round_epi<__nv_bfloat16>(float v) {
+  uint32_t u = __float_as_uint(v);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return __uint_as_float(u & 0xFFFF0000u);
+}
+template <> __device__ __forceinline__ float round_epi<__half>(float v) { return round_to<__half>(v); }
+// Pack two values that are already exact in T (high halves for bf16).
+template <typename T> __device__ __forceinline__ uint32_t pack_exact2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack_exact2<__nv_bfloat16>(float a, float b) {
+  return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+}
+template <> __device__ __forceinline__ uint32_t pack_exact2<__half>(float a, float b) { return pack2<__half>(a, b); }
+
 // Two 16-bit values of a packed word as floats (low half first).
 template <typename T> __device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
 template <> __device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {

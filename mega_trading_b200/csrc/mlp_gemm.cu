@@ -251,11 +251,11 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             // projections rounded to the activation dtype, as the GEMM output is
-            const float g0 = round_to<T>(__uint_as_float(zg[i])), g1 = round_to<T>(__uint_as_float(zg[i + 1]));
-            const float u0 = round_to<T>(__uint_as_float(zu[i])), u1 = round_to<T>(__uint_as_float(zu[i + 1]));
-            pg[i >> 1] = pack2<T>(g0, g1);
-            pu[i >> 1] = pack2<T>(u0, u1);
-            py[i >> 1] = pack2<T>(round_to<T>(g0 * sigmoid_f32(g0)) * u0, round_to<T>(g1 * sigmoid_f32(g1)) * u1);
+            const float g0 = round_epi<T>(__uint_as_float(zg[i])), g1 = round_epi<T>(__uint_as_float(zg[i + 1]));
+            const float u0 = round_epi<T>(__uint_as_float(zu[i])), u1 = round_epi<T>(__uint_as_float(zu[i + 1]));
+            pg[i >> 1] = pack_exact2<T>(g0, g1);
+            pu[i >> 1] = pack_exact2<T>(u0, u1);
+            py[i >> 1] = pack2<T>(round_epi<T>(g0 * sigmoid_f32(g0)) * u0, round_epi<T>(g1 * sigmoid_f32(g1)) * u1);
           }
           // this warpgroup's previous stores must have finished reading its staging boxes
           if (r == 0) bulk_wait_group_read0();
@@ -310,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                   const int i = h * 8 + w * 2 + e;  // pair index within the chunk
-                  const float ev = round_to<T>(__uint_as_float(z[2 * i]));
-                  const float od = round_to<T>(__uint_as_float(z[2 * i + 1]));
+                  const float ev = round_epi<T>(__uint_as_float(z[2 * i]));
+                  const float od = round_epi<T>(__uint_as_float(z[2 * i + 1]));
                   pk[i] = pack2<T>(ev * cs[e] - od * sn[e], ev * sn[e] + od * cs[e]);
                 }
               }
@@ -366,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
             unpack2<T>(uw[i], u[0], u[1]);
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float dy = round_to<T>(__uint_as_float(zd[2 * i + e]));  // dY is a bf16 GEMM output
+              const float dy = round_epi<T>(__uint_as_float(zd[2 * i + e]));  // dY is a bf16 GEMM output
               const float s = sigmoid_f32(g[e]);
               o_g[e] = dy * u[e] * s * (1.f + g[e] * (1.f - s));
-              o_u[e] = dy * round_to<T>(g[e] * s);
+              o_u[e] = dy * round_epi<T>(g[e] * s);
             }
             pg[i] = pack2<T>(o_g[0], o_g[1]);
             pu[i] = pack2<T>(o_u[0], o_u[1]);
