@@ -28,9 +28,13 @@ DEMO = dict(vocab_size=21504, block_size=512, hidden_dim=256, layers=4, attentio
             intermediate_dim=688, rope_theta=10_000.0)
 GQA12_SMALL = dict(vocab_size=21504, block_size=1024, hidden_dim=768, layers=2, attention_heads=12, kv_heads=4,
                    intermediate_dim=2048)
+# BASELINE config 4's layer shapes (d_model 1024, 16/4 heads, SwiGLU 2816) at its
+# sequence length 4096, two layers
+LARGE24_SLICE = dict(vocab_size=21504, block_size=4096, hidden_dim=1024, layers=2, attention_heads=16, kv_heads=4,
+                     intermediate_dim=2816)
 
 
-@pytest.mark.parametrize("cfg_kwargs,batch,seq", [(DEMO, 2, 512), (GQA12_SMALL, 1, 1024)])
+@pytest.mark.parametrize("cfg_kwargs,batch,seq", [(DEMO, 2, 512), (GQA12_SMALL, 1, 1024), (LARGE24_SLICE, 1, 4096)])
 def test_model_loss_and_grads_match_oracle(cuda_device, cfg_kwargs, batch, seq):
     from mega_trading_b200 import _lib
     from mega_trading_b200.data import next_token_batch
