@@ -83,7 +83,7 @@ def test_fused_blocks_reject_bad_input(cuda_device):
 
 
 @pytest.mark.parametrize("M,H,I,seed", [(4096, 768, 2048, 61), (300, 256, 512, 62), (1, 768, 256, 63),
-                                        (1000, 64, 768, 64)])
+                                        (1000, 64, 768, 64), (513, 200, 256, 66)])
 def test_swiglu_mlp_matches_oracle(cuda_device, M, H, I, seed):
     """Fused SwiGLU MLP (gate inside the tcgen05 GEMM epilogues) vs the fp32 oracle."""
     from mega_trading_b200.kernels.fused_blocks import interleave_gate_up, swiglu_mlp
@@ -141,7 +141,8 @@ def test_swiglu_gemm_gate_is_bit_exact_with_the_standalone_gate(cuda_device):
 
 @pytest.mark.parametrize("B,T,H,Hq,Hkv,D,theta,seed", [(2, 256, 768, 12, 4, 64, 500_000.0, 71),
                                                        (1, 300, 256, 8, 4, 32, 10_000.0, 72),
-                                                       (3, 128, 512, 4, 2, 64, 10_000.0, 73)])
+                                                       (3, 128, 512, 4, 2, 64, 10_000.0, 73),
+                                                       (1, 77, 200, 4, 2, 64, 10_000.0, 75)])
 def test_qkv_proj_rope_attention_matches_oracle(cuda_device, B, T, H, Hq, Hkv, D, theta, seed):
     """Projection GEMM with RoPE in its epilogue + attention, vs the fp32 oracle chain."""
     from mega_trading_b200.kernels.fused_blocks import qkv_proj_rope_attention

@@ -87,3 +87,33 @@ def test_clock_sampler_summary_parses_nvidia_smi_rows(tmp_path):
                       "0, 1800, 1965, 990.1, 0x4, Not Active, Not Active, Not Active, Active\n")
     out = s.summary()
     assert out["sm_max_mhz"] == 1965.0 and out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
+
+
+def test_gate_up_interleave_layout():
+    """The fused SwiGLU weight alternates 128-row blocks of w1 and w3, and
+    its gradient routes back to the right rows of each."""
+    from mega_trading_b200.kernels.fused_blocks import interleave_gate_up, swiglu_mlp_supported
+
+    w1 = torch.arange(512 * 4, dtype=torch.float32).view(512, 4).requires_grad_(True)
+    w3 = (-torch.arange(512 * 4, dtype=torch.float32)).view(512, 4).requires_grad_(True)
+    w13 = interleave_gate_up(w1, w3)
+    assert w13.shape == (1024, 4)
+    for b in range(4):
+        assert torch.equal(w13[256 * b:256 * b + 128], w1[128 * b:128 * (b + 1)])
+        assert torch.equal(w13[256 * b + 128:256 * (b + 1)], w3[128 * b:128 * (b + 1)])
+    g = torch.randn_like(w13)
+    w13.backward(g)
+    for b in range(4):
+        assert torch.equal(w1.grad[128 * b:128 * (b + 1)], g[256 * b:256 * b + 128])
+        assert torch.equal(w3.grad[128 * b:128 * (b + 1)], g[256 * b + 128:256 * (b + 1)])
+    assert swiglu_mlp_supported(2048, 768) and swiglu_mlp_supported(2816, 1024)
+    assert not swiglu_mlp_supported(688, 256)
+
+
+def test_fused_projection_paths_follow_the_shapes():
+    from mega_trading_b200.kernels.fused_blocks import qkv_rope_gemm_supported
+
+    assert qkv_rope_gemm_supported(12, 4, 64, 768)      # config 3: 1280 columns
+    assert qkv_rope_gemm_supported(16, 4, 64, 1024)     # config 4: 1536 columns
+    assert not qkv_rope_gemm_supported(8, 2, 32, 256)   # config 0: 384 columns -> cuBLAS + RoPE kernel
+    assert not qkv_rope_gemm_supported(4, 2, 48, 256)   # head_dim 48
