@@ -78,7 +78,7 @@ struct BwdCfg {
 struct BwdParams {
   CUtensorMap tm_q, tm_k, tm_v, tm_do, tm_dq;  // tm_dq: fp32 accumulator [rows, D]
   int sw_q, sw_k, sw_v, sw_do;                 // coordinate order of each bf16 map
-  const float* lse2;                           // [B*Hq*Tp] lse * log2(e), +inf past T
+  const float* lse2;                           // [B*Hq*Tp] -lse * log2(e), -inf past T
   const float* delta;                          // [B*Hq*Tp]
   void* dk;
   void* dv;
@@ -441,16 +441,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           lv[i] = a.x; lv[i + 1] = a.y; lv[i + 2] = a.z; lv[i + 3] = a.w;
           dlv[i] = d.x; dlv[i + 1] = d.y; dlv[i + 2] = d.z; dlv[i + 3] = d.w;
         }
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lv[i]));
-          float p1 = fast_exp2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -lv[i + 1]));
+          // P = exp2(s * scale * log2e - lse * log2e), dS = P (dP - delta), two lanes per instruction
+          const float2 x = fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2,
+                                make_float2(lv[i], lv[i + 1]));
+          float p0 = fast_exp2(x.x);
+          float p1 = fast_exp2(x.y);
           if (diag) {
             if (i < lim) p0 = 0.f;
             if (i + 1 < lim) p1 = 0.f;
           }
-          const float d0 = p0 * (__uint_as_float(dv[i]) - dlv[i]);
-          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dlv[i + 1]);
+          const float2 dd = mul2(make_float2(p0, p1), sub2(make_float2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])),
+                                                           make_float2(dlv[i], dlv[i + 1])));
+          const float d0 = dd.x, d1 = dd.y;
           if (c < 2)
             pk0[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
           else
@@ -566,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
-// preprocess: delta = rowsum(O * dO), lse2 = lse * log2(e) (+inf past T)
+// preprocess: delta = rowsum(O * dO), lse2 = -lse * log2(e) (-inf past T: P = 0
+// there), stored negated so the probability is one fma + ex2
 // 8 (D=64) or 4 (D=32) lanes per row, 16-byte loads.
 // ---------------------------------------------------------------------------
 template <typename T, int D>
@@ -595,7 +601,7 @@ __global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, con
   for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (valid_row && sub == 0) {
     delta[row] = acc;
-    lse2[row] = (t < seq) ? lse[bh * seq + t] * 1.4426950408889634f : INFINITY;
+    lse2[row] = (t < seq) ? lse[bh * seq + t] * -1.4426950408889634f : -INFINITY;
   }
 }
 
