@@ -62,6 +62,13 @@ MT_API const char* mt_last_error(void);
  *   bit layout: (kernel_id << 16) | wait_site
  */
 
+/* Timing hook (no counterpart in the reference).  Two caller-owned CUDA
+ * events (CUevent / cudaEvent_t handles, created by the caller) that the next
+ * calls on this host thread record on their stream right before and right
+ * after their main kernel (the tcgen05 attention kernels), so a caller can time
+ * that kernel alone inside a multi-kernel operator.  Both NULL disables it. */
+MT_API int mt_set_timing_events(void* before_main, void* after_main);
+
 /* ---------------------------------------------------------------------
  * RMSNorm   replaces triton_rms_norm (src/mega_trading/kernels/triton_ops.py:11-15,
  *           forward kernel :528-538, backward :633-665 + torch sum :183)

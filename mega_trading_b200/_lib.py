@@ -58,6 +58,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "mt_swiglu_gemm_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "mt_qkv_rope_gemm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                  c_vp, c_vp]),
+    "mt_set_timing_events": (c_int, [c_vp, c_vp]),
     "mt_rope": (
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64p, c_i64p, c_i64p,
@@ -203,17 +204,29 @@ class KernelTimer:
     def reset(self) -> None:
         self.events = {}
 
-    def start(self, name: str, device: torch.device):
+    def start(self, name: str, device: torch.device, main_kernel: bool = False):
+        """Events around the whole call; with ``main_kernel`` also events the library records
+        around the call's main kernel (mt_set_timing_events), kept as ``name + "_kernel"``."""
         if not self.enabled:
             return None
+        stream = torch.cuda.current_stream(device)
         ev = torch.cuda.Event(enable_timing=True)
-        ev.record(torch.cuda.current_stream(device))
-        return (name, ev, device)
+        ev.record(stream)
+        inner = None
+        if main_kernel:
+            inner = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for e in inner:  # create the driver events; the library re-records them
+                e.record(stream)
+            _check_hook(load().mt_set_timing_events(inner[0].cuda_event, inner[1].cuda_event))
+        return (name, ev, device, inner)
 
     def stop(self, token) -> None:
         if token is None:
             return
-        name, ev, device = token
+        name, ev, device, inner = token
+        if inner is not None:
+            _check_hook(load().mt_set_timing_events(None, None))
+            self.events.setdefault(name + "_kernel", []).append(inner)
         end = torch.cuda.Event(enable_timing=True)
         end.record(torch.cuda.current_stream(device))
         self.events.setdefault(name, []).append((ev, end))
@@ -226,6 +239,11 @@ class KernelTimer:
             total = sum(a.elapsed_time(b) for a, b in pairs)
             out[name] = (len(pairs), total / max(len(pairs), 1))
         return out
+
+
+def _check_hook(st: int) -> None:
+    if st != 0:
+        raise B200KernelError(f"mt_set_timing_events failed (status {st})")
 
 
 timer = KernelTimer()

@@ -679,7 +679,9 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
     prm.group = (int)(g < 1 ? 1 : (g > prm.n_heads ? prm.n_heads : g));
     const int64_t blocks = int64_t(prm.n_heads) * prm.n_tiles;
     if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+    record_timing_event(0, stream);
     kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
+    record_timing_event(1, stream);
     st = check_launch("attention_bwd");
     if (st != MT_OK) return st;
   }

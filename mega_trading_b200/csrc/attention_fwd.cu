@@ -394,7 +394,9 @@ int launch_fwd(const FwdParams& prm, int B, int Hq, cudaStream_t stream) {
   if (st != MT_OK) return st;
   const int64_t blocks = int64_t(B) * Hq * prm.n_pairs;
   if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+  record_timing_event(0, stream);
   kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
+  record_timing_event(1, stream);
   return check_launch("attention_fwd");
 }
 

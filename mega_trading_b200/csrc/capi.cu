@@ -71,6 +71,17 @@ EncodeTiledFn g_encode = nullptr;
 typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 CtxGetCurrentFn g_ctx_get_current = nullptr;
 
+// Timing events of the calling thread (driver handles owned by the caller).
+typedef CUresult (*EventRecordFn)(CUevent, CUstream);
+EventRecordFn g_event_record = nullptr;
+thread_local CUevent t_timing_events[2] = {nullptr, nullptr};
+
+void record_timing_event(int which, cudaStream_t stream) {
+  CUevent ev = t_timing_events[which & 1];
+  if (ev == nullptr || g_event_record == nullptr) return;
+  g_event_record(ev, reinterpret_cast<CUstream>(stream));
+}
+
 int bind_device_of(const void* ptr) {
   // A thread that has not touched CUDA yet (e.g. PyTorch's autograd worker
   // for device 0) may have no current context; the driver-API tensor-map
@@ -196,3 +207,22 @@ int mt_built_arch(void) { return 100; }
 const char* mt_last_error(void) { return mt::g_last_error; }
 
 }  // extern "C"
+
+extern "C" int mt_set_timing_events(void* before_main, void* after_main) {
+  using namespace mt;
+  if ((before_main == nullptr) != (after_main == nullptr)) return MT_ERR_INVALID_ARGUMENT;
+  if (before_main != nullptr && g_event_record == nullptr) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_event_record == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuEventRecord", &fn, cudaEnableDefault, &q) != cudaSuccess || fn == nullptr)
+        return MT_ERR_LAUNCH;
+      g_event_record = reinterpret_cast<EventRecordFn>(fn);
+    }
+  }
+  t_timing_events[0] = static_cast<CUevent>(before_main);
+  t_timing_events[1] = static_cast<CUevent>(after_main);
+  return MT_OK;
+}
+

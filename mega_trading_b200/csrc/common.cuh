@@ -26,6 +26,10 @@ int get_sm_count();
 // Raise the dynamic shared memory limit of a kernel (once per device and
 // kernel) when a launch needs more than the default 48 KB.
 int set_smem_limit(const void* func, int bytes);
+// Optional caller-owned events (driver handles) recorded right around the
+// main kernel of an operator, for callers that time that kernel alone
+// (mt_set_timing_events); no-ops when unset.  Per host thread.
+void record_timing_event(int which, cudaStream_t stream);
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank,
                       void* base, const uint64_t* dims,

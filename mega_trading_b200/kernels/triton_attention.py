@@ -28,7 +28,7 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     o = torch.empty_like(q)
     lse = torch.empty((B, Hq, T), device=q.device, dtype=torch.float32)
     status = _lib.status_word(q.device)
-    tok = _lib.timer.start("attention_fwd", q.device)
+    tok = _lib.timer.start("attention_fwd", q.device, main_kernel=True)
     st = lib.mt_attention_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), _lib.dtype_code(q.dtype),
         B, Hq, Hkv, T, D, _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
@@ -52,7 +52,7 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None, ro
     ws_bytes = int(lib.mt_attention_bwd_workspace_bytes(B, Hq, T, D))
     ws = torch.empty((max(ws_bytes, 16),), device=q.device, dtype=torch.uint8)
     status = _lib.status_word(q.device)
-    tok = _lib.timer.start("attention_bwd", q.device)
+    tok = _lib.timer.start("attention_bwd", q.device, main_kernel=True)
     common = (
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), do.data_ptr(), dq.data_ptr(),
         dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), B, Hq, Hkv, T, D,

@@ -116,3 +116,30 @@ def test_attention_backward_matches_oracle(cuda_device, B, Hq, Hkv, T, D, dtype,
     _check(qd.grad, qo.grad, "attention dq", atol=8e-2)
     _check(kd.grad, ko.grad, "attention dk", atol=8e-2)
     _check(vd.grad, vo.grad, "attention dv", atol=8e-2)
+
+
+def test_timing_hook_times_the_main_kernel(cuda_device):
+    """mt_set_timing_events: the library records caller events around its main
+    attention kernels; that time is positive and within the whole call's."""
+    from mega_trading_b200 import _lib
+    from mega_trading_b200.kernels import triton_attention as A
+
+    g = torch.Generator(device=cuda_device).manual_seed(81)
+    q = torch.randn(4, 8, 1024, 64, device=cuda_device, generator=g).bfloat16()
+    k = torch.randn(4, 2, 1024, 64, device=cuda_device, generator=g).bfloat16()
+    v = torch.randn(4, 2, 1024, 64, device=cuda_device, generator=g).bfloat16()
+    _lib.timer.reset()
+    _lib.timer.enabled = True
+    try:
+        o, lse = A._launch_fwd(q, k, v, 4, 0.125)
+        A._launch_bwd(q, k, v, o, lse, torch.ones_like(o), 0.125)
+    finally:
+        _lib.timer.enabled = False
+    s = _lib.timer.summary()
+    for name in ("attention_fwd", "attention_bwd"):
+        n_all, ms_all = s[name]
+        n_k, ms_k = s[name + "_kernel"]
+        assert n_all == n_k == 1
+        assert 0.0 < ms_k <= ms_all
+    # the hook is cleared after each call: a plain call records nothing
+    assert _lib.load().mt_set_timing_events(None, None) == 0
