@@ -572,13 +572,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
 
 // ---------------------------------------------------------------------------
 // preprocess: delta = rowsum(O * dO), lse2 = -lse * log2(e) (-inf past T: P = 0
-// there), stored negated so the probability is one fma + ex2
+// there), stored negated so the probability is one fma + ex2; zeroes the fp32
+// dQ accumulator rows
 // 8 (D=64) or 4 (D=32) lanes per row, 16-byte loads.
 // ---------------------------------------------------------------------------
 template <typename T, int D>
 __global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, const T* __restrict__ dout,
                                                     const float* __restrict__ lse, float* __restrict__ delta,
-                                                    float* __restrict__ lse2, int64_t os0, int64_t os1, int64_t os2,
+                                                    float* __restrict__ lse2, float* __restrict__ dq_acc,
+                                                    int64_t os0, int64_t os1, int64_t os2,
                                                     int64_t ds0, int64_t ds1, int64_t ds2, int Hq, int seq, int Tp,
                                                     int64_t rows) {
   constexpr int LPR = D / 8;  // lanes per row
@@ -599,6 +601,11 @@ __global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, con
   }
 #pragma unroll
   for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (valid_row) {  // the fp32 dQ accumulator starts at zero
+    float4* z = reinterpret_cast<float4*>(dq_acc + row * D + sub * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (valid_row && sub == 0) {
     delta[row] = acc;
     lse2[row] = (t < seq) ? lse[bh * seq + t] * -1.4426950408889634f : -INFINITY;
@@ -655,15 +662,10 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
             const int64_t* dos, const int64_t* dqs, Workspace& ws, int B, cudaStream_t stream) {
   using C = BwdCfg<D>;
   const int64_t rows = int64_t(B) * prm.Hq * prm.Tp;
-  cudaError_t e = cudaMemsetAsync(ws.dq_acc, 0, rows * D * 4, stream);
-  if (e != cudaSuccess) {
-    set_last_error("cudaMemsetAsync(dq_acc)", e);
-    return MT_ERR_LAUNCH;
-  }
   {
     const int64_t threads = rows * (D / 8);
     attn_bwd_pre<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const T*>(o), static_cast<const T*>(dout), lse, ws.delta, ws.lse2, os[0], os[1], os[2], dos[0],
+        static_cast<const T*>(o), static_cast<const T*>(dout), lse, ws.delta, ws.lse2, ws.dq_acc, os[0], os[1], os[2], dos[0],
         dos[1], dos[2], prm.Hq, prm.T, prm.Tp, rows);
     int st = check_launch("attention_bwd_pre");
     if (st != MT_OK) return st;
