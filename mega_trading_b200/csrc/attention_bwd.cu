@@ -308,7 +308,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
         // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
 #pragma unroll
         for (int kk = 0; kk < kBQ / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
           const uint32_t b_off = kk * 16 * C::ROW_BYTES;
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),

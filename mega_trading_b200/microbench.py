@@ -33,7 +33,6 @@ import torch
 from . import _lib
 from .kernels import triton_attention as A
 from .kernels import triton_ops as K
-from .kernels.fused_ce import _FusedLinearCrossEntropy  # noqa: F401  (autograd path used below)
 
 ROOT = Path(__file__).resolve().parent.parent
 

@@ -66,7 +66,7 @@ def test_composite_tokens_distribution():
     assert torch.equal(composite_tokens(3, 5, seed=4), composite_tokens(3, 5, seed=4))
 
 
-def test_flop_accounting_matches_survey():
+def test_flop_accounting_per_token_and_step():
     from mega_trading_b200.model import CONFIGS
 
     cfg = CONFIGS["gqa12"]
