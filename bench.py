@@ -197,6 +197,7 @@ def main(argv: list[str] | None = None) -> int:
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    torch.cuda.reset_peak_memory_stats(device)
     for _ in range(max(args.warmup, 0)):
         trainer.step(ids, labels)
     torch.cuda.synchronize()
@@ -320,6 +321,7 @@ def main(argv: list[str] | None = None) -> int:
                     "d2h_bytes_per_step": 4, "steps": e2e_steps,
                     "note": "per rank: pinned host tokens copied to HBM and the loss read back every step"},
             "gpu_launches": launches,
+            "peak_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
             "device_status": status,
             "clocks": clock_summary,
             "last_loss": float(loss_host),
