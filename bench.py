@@ -50,7 +50,9 @@ def _peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms during the timed region:
+    entering waits (up to 5 s) for the first sample, and only samples written after
+    ``mark()`` (called right before timing starts) are summarised."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -60,15 +62,29 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+        self.skip = 0
+
+    def _lines(self) -> list[str]:
+        try:
+            return self.path.read_text().splitlines()
+        except OSError:
+            return []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
+        t0 = time.time()
+        while self.proc is not None and not self._lines() and time.time() - t0 < 5.0:
+            time.sleep(0.02)
         return self
+
+    def mark(self) -> None:
+        """Samples from here on belong to the timed region."""
+        self.skip = len(self._lines())
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -81,7 +97,7 @@ class ClockSampler:
     def summary(self) -> dict:
         rows = []
         try:
-            for line in self.path.read_text().splitlines():
+            for line in self._lines()[self.skip:]:
                 parts = [x.strip() for x in line.split(",")]
                 if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
                     rows.append(parts)
@@ -211,6 +227,7 @@ def main(argv: list[str] | None = None) -> int:
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        clocks.mark()
         start.record(stream)
         for _ in range(args.steps):
             loss = trainer.step(ids, labels)

@@ -89,6 +89,19 @@ def test_clock_sampler_summary_parses_nvidia_smi_rows(tmp_path):
     assert out["sm_max_mhz"] == 1965.0 and out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
 
 
+def test_clock_sampler_counts_only_samples_after_the_mark(tmp_path):
+    import bench
+
+    s = bench.ClockSampler(0)
+    s.path = tmp_path / "c.csv"
+    s.path.write_text("0, 1965, 1965, 100.0, 0x0, Not Active, Not Active, Not Active, Not Active\n")
+    s.mark()  # timing starts: the idle sample above is not part of the region
+    with s.path.open("a") as f:
+        f.write("0, 1500, 1965, 998.0, 0x4, Not Active, Not Active, Not Active, Active\n")
+    out = s.summary()
+    assert out["samples"] == 1 and out["sm_mhz"] == 1500.0 and out["reasons"] == ["sw_power_cap"]
+
+
 def test_gate_up_interleave_layout():
     """The fused SwiGLU weight alternates 128-row blocks of w1 and w3, and
     its gradient routes back to the right rows of each."""
