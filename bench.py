@@ -5,9 +5,11 @@ full training steps of BASELINE config 3 -- 12 layers, d_model 768, 12/4 GQA
 heads, head_dim 64, SwiGLU 2048, vocab 21,504, seq 2048, global batch 256
 sequences split over the N ranks (strong scaling), bf16 GEMMs with fp32
 master weights and fused AdamW -- on seeded synthetic composite-token streams
-already resident in HBM.  One JSON line on rank 0 (see the contract fields
-below).  ``--impl reference`` times the reference's own PyTorch path
-(the CPU fp32 restatement in ``oracle/``) on the host cores instead.
+already resident in HBM.  ``--model large24`` runs BASELINE config 4 instead
+(24 layers, d_model 1024, 16/4 GQA heads, SwiGLU 2816, seq 4096, global batch
+128).  One JSON line on rank 0 (see the contract fields below).
+``--impl reference`` times the reference's own PyTorch path (the CPU fp32
+restatement in ``oracle/``) on the host cores instead.
 """
 
 from __future__ import annotations
@@ -29,15 +31,33 @@ sys.path.insert(0, str(ROOT))
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-METRIC = "train tokens/s (config 3: 12L d768 GQA 12/4, seq 2048, global batch 256)"
-GLOBAL_BATCH = 256
-SEQ = 2048
-MICRO_BATCH = 128
+# training workloads: model key in mega_trading_b200.model.CONFIGS, global batch,
+# sequence length, default micro-batch per rank
+WORKLOADS = {
+    "gqa12": {"metric": "train tokens/s (config 3: 12L d768 GQA 12/4, seq 2048, global batch 256)",
+              "workload": "config3_train_step", "global_batch": 256, "seq": 2048, "micro_batch": 128,
+              "model": "12L d768 Hq12/Hkv4 D64 I2048 V21504"},
+    "large24": {"metric": "train tokens/s (config 4: 24L d1024 GQA 16/4, seq 4096, global batch 128)",
+                "workload": "config4_train_step", "global_batch": 128, "seq": 4096, "micro_batch": 32,
+                "model": "24L d1024 Hq16/Hkv4 D64 I2816 V21504"},
+}
 CPU_SAMPLE_SEQS = 1
 # DRAM bytes (read + write) of one attn_bwd_kernel launch measured by ncu at
 # B=128, Hq=12, Hkv=4, T=2048, D=64 (profiles/attention_bwd_config3_layer.txt);
 # traffic grows with the batch, so a launch of B sequences moves B/128 times this.
-ATTN_BWD_DRAM_BYTES = (1_904_392_192 + 1_030_479_616, 128)
+# Keyed by the workload whose shape it was captured on.
+ATTN_BWD_DRAM_BYTES = {"gqa12": (1_904_392_192 + 1_030_479_616, 128)}
+
+
+def _ref_config(name: str):
+    """The oracle model configuration for a workload (same fields as the product's)."""
+    from dataclasses import asdict
+
+    from oracle.model import ModelConfig as RefCfg
+
+    from mega_trading_b200.model import CONFIGS
+
+    return RefCfg(**asdict(CONFIGS[name]))
 
 
 def _peaks() -> dict:
@@ -112,9 +132,9 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, budget_s: float = 12.0) -> dict:
+def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, budget_s: float = 12.0,
+                           model_name: str = "gqa12") -> dict:
     """The reference's PyTorch train step (oracle/ CPU fp32 restatement) on the host cores."""
-    from oracle.model import ModelConfig as RefCfg
     from oracle.model import TradingModelRef, make_optimizer, train_step
 
     from mega_trading_b200.data import next_token_batch
@@ -122,7 +142,7 @@ def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, bu
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     torch.manual_seed(0)
-    model = TradingModelRef(RefCfg())
+    model = TradingModelRef(_ref_config(model_name))
     opt = make_optimizer(model)
     ids, labels = next_token_batch(seqs, seq_len, seed=7, device="cpu")
     train_step(model, opt, ids, labels)  # warm-up
@@ -139,7 +159,8 @@ def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, bu
     tok = seqs * seq_len
     return {"value": tok / statistics.mean(times), "unit": "tokens/s", "cores": torch.get_num_threads(),
             "kind": "port", "steps": len(times),
-            "sample": f"{seqs} x {seq_len}-token sequence(s) per step of the config-3 model, fp32, full step "
+            "sample": f"{seqs} x {seq_len}-token sequence(s) per step of the {WORKLOADS[model_name]['model']} "
+                      "model, fp32, full step "
                       f"(forward, CE, backward, AdamW); {len(times)} timed step(s)"}
 
 
@@ -148,14 +169,15 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     steps, warm = args.steps, args.warmup
-    from oracle.model import ModelConfig as RefCfg
+    wl = WORKLOADS[args.model]
+    SEQ = wl["seq"]
     from oracle.model import TradingModelRef, make_optimizer, train_step
 
     from mega_trading_b200.data import next_token_batch
 
     torch.set_num_threads(os.cpu_count() or 1)
     torch.manual_seed(0)
-    model = TradingModelRef(RefCfg())
+    model = TradingModelRef(_ref_config(args.model))
     opt = make_optimizer(model)
     ids, labels = next_token_batch(CPU_SAMPLE_SEQS, SEQ, seed=7, device="cpu")
     for _ in range(warm):
@@ -167,14 +189,14 @@ def run_reference(args) -> None:
     tok = CPU_SAMPLE_SEQS * SEQ
     value = tok * steps / el
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": wl["metric"], "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic composite-token streams",
-        "config": {"workload": "config3_train_step", "model": "12L d768 Hq12/Hkv4 D64 I2048 V21504",
+        "config": {"workload": wl["workload"], "model": wl["model"],
                    "global_batch": CPU_SAMPLE_SEQS, "seq_len": SEQ, "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"{CPU_SAMPLE_SEQS} x {SEQ}-token sequence per step (bounded sample of the "
-                                   "global batch of 256), fp32 forward+CE+backward+AdamW"},
+                                   f"global batch of {wl['global_batch']}), fp32 forward+CE+backward+AdamW"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -186,7 +208,9 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--micro-batch", type=int, default=MICRO_BATCH)
+    ap.add_argument("--model", choices=tuple(WORKLOADS), default="gqa12",
+                    help="gqa12 = BASELINE config 3 (default), large24 = config 4")
+    ap.add_argument("--micro-batch", type=int, default=None, help="sequences per micro-step and rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.impl == "reference":
@@ -198,14 +222,16 @@ def main(argv: list[str] | None = None) -> int:
     from mega_trading_b200.model import CONFIGS
     from mega_trading_b200.train import Trainer, init_distributed
 
+    wl = WORKLOADS[args.model]
+    METRIC, GLOBAL_BATCH, SEQ = wl["metric"], wl["global_batch"], wl["seq"]
     rank, world, local = init_distributed("nccl")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if GLOBAL_BATCH % world:
         raise SystemExit(f"global batch {GLOBAL_BATCH} is not divisible by {world} ranks")
-    cfg = CONFIGS["gqa12"]
+    cfg = CONFIGS[args.model]
     local_batch = GLOBAL_BATCH // world
-    micro = min(args.micro_batch, local_batch)
+    micro = min(args.micro_batch or wl["micro_batch"], local_batch)
     trainer = Trainer(cfg, micro_batch=micro, device=device)
     ids, labels = next_token_batch(local_batch, SEQ, seed=1000 + rank, device=device)
 
@@ -280,6 +306,12 @@ def main(argv: list[str] | None = None) -> int:
     rows_q = B * cfg.attention_heads * SEQ
     rows_kv = B * cfg.kv_heads * SEQ
     attn_bwd_bytes = (3 * rows_q + 4 * rows_kv) * cfg.head_dim * 2 + rows_q * 8
+    if args.model in ATTN_BWD_DRAM_BYTES:
+        cap_bytes, cap_b = ATTN_BWD_DRAM_BYTES[args.model]
+        traffic = cap_bytes * B / cap_b
+        traffic_source = f"ncu dram__bytes_read+write of one launch at B={cap_b}, scaled by B={B}"
+    else:
+        traffic, traffic_source = None, f"no ncu capture of this kernel at the {wl['workload']} shape"
     kernels = {name: {"launches": n, "mean_ms": ms} for name, (n, ms) in kern.items()}
     for name, fl in (("attention_fwd", fwd_flops), ("attention_bwd", bwd_flops)):
         for key in (name, name + "_kernel"):
@@ -294,7 +326,7 @@ def main(argv: list[str] | None = None) -> int:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_train_tokens_per_s(CPU_SAMPLE_SEQS, SEQ)
+        cpu = cpu_train_tokens_per_s(CPU_SAMPLE_SEQS, SEQ, model_name=args.model)
 
     if rank == 0:
         line = {
@@ -311,8 +343,8 @@ def main(argv: list[str] | None = None) -> int:
             "dtype": "bf16",
             "data": "synthetic composite-token streams (seeded, BASELINE distribution), generated on device",
             "config": {
-                "workload": "config3_train_step",
-                "model": "12L d768 Hq12/Hkv4 D64 I2048 V21504 (dropout 0, tied embeddings)",
+                "workload": wl["workload"],
+                "model": wl["model"] + " (dropout 0, tied embeddings)",
                 "global_batch": GLOBAL_BATCH, "seq_len": SEQ, "micro_batch": micro,
                 "grad_accum": math.ceil(local_batch / micro), "parallelism": f"dp{world}",
                 "optimizer": "fused AdamW, fp32 master weights",
@@ -325,9 +357,8 @@ def main(argv: list[str] | None = None) -> int:
                 "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"] + " (sustained bf16: the kernel runs inside a long step)",
-                "traffic": ATTN_BWD_DRAM_BYTES[0] * B / ATTN_BWD_DRAM_BYTES[1],
-                "traffic_source": f"ncu dram__bytes_read+write of one launch at B={ATTN_BWD_DRAM_BYTES[1]}, "
-                                  f"scaled by B={B}",
+                "traffic": traffic,
+                "traffic_source": traffic_source,
                 "algorithmic_flops_per_launch": bwd_flops,
                 "algorithmic_bytes_per_launch": attn_bwd_bytes,
             },

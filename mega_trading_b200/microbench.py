@@ -1,6 +1,6 @@
 """Per-operator microbenchmarks at the BASELINE operator shapes.
 
-``python -m mega_trading_b200.microbench [--ops attention,ce,rmsnorm,rope,swiglu] [--iters N]``
+``python -m mega_trading_b200.microbench [--ops attention,ce,rmsnorm,addrmsnorm,rope,swiglu] [--iters N]``
 
 * attention: config 1 -- B=16, Hq=16, Hkv=4, D=64, T in {1024, 2048, 4096}
   (``--batch 32 --heads 12 --kv-heads 4 --seqs 2048`` is one config-3 layer),
@@ -13,8 +13,11 @@
   F.rms_norm, eager RoPE, F.silu * up, F.linear + F.cross_entropy).
 * mlp: the SwiGLU GEMMs with the gate in the epilogue (2NH*2I forward,
   2NHI backward) against cuBLAS + the standalone packed gate.
-* rmsnorm / rope / swiglu: config 2 token count, HBM GB/s of the algorithmic
-  bytes (each input read once, each output written once).
+* rmsnorm / addrmsnorm / rope / swiglu: config 2 token count, HBM GB/s of the
+  algorithmic bytes (each input read once, each output written once).
+  addrmsnorm runs the fused residual add + RMSNorm twice: all-bf16 (config 2)
+  and the training step's mix (bf16 branch, fp32 residual stream, bf16 normed
+  output; the backward also writes the bf16 branch gradient).
 
 Times are CUDA-event means on the launching stream after warm-up; inputs are
 regenerated per case and exceed L2 except where noted.  ``--profile`` runs
@@ -123,7 +126,45 @@ def ce_cases(dev, iters, profile, n=65536, h=768, v=21504):
              "grad_logits_bytes_written": n * v * 2}]
 
 
-def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65536):
+def _add_rms_case(dev, g, n, H, res_dtype, iters, profile) -> dict | None:
+    """Fused residual add + RMSNorm forward and backward at one dtype mix."""
+    lib = _lib.load()
+    bf = torch.bfloat16
+    x = torch.randn(n, H, device=dev, generator=g).to(bf)
+    r = torch.randn(n, H, device=dev, generator=g).to(res_dtype)
+    # the weight follows the residual stream (fp32 master weight in the training step)
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).to(res_dtype)
+    new_res, normed = torch.empty_like(r), torch.empty(n, H, device=dev, dtype=bf)
+    rstd = torch.empty(n, device=dev, dtype=torch.float32)
+    gres = torch.randn(n, H, device=dev, generator=g).to(res_dtype)
+    gn = torch.randn(n, H, device=dev, generator=g).to(bf)
+    st = _lib.stream_ptr(dev)
+
+    def f():
+        _lib.check(lib.mt_add_rms_norm_fwd(x.data_ptr(), r.data_ptr(), _lib.dtype_code(bf), w.data_ptr(),
+                                           _lib.dtype_code(res_dtype), new_res.data_ptr(), _lib.dtype_code(res_dtype),
+                                           normed.data_ptr(), _lib.dtype_code(bf), rstd.data_ptr(), n, H, 1e-5, st),
+                   "add_rms_norm forward")
+
+    f()
+    b = lambda: K._rms_bwd(new_res, w, rstd, gn, res_dtype, residual_grad=gres, branch_dtype=bf)  # noqa: E731
+    if profile:
+        for _ in range(iters):
+            f()
+            b()
+        return None
+    rb, hb = r.element_size(), 2
+    # forward: hidden + residual in, new residual + normed out, rstd out
+    # backward: new residual, its gradient and the normed gradient in; the residual
+    # gradient (and the narrower branch copy when the dtypes differ) out
+    byts_f = n * H * (hb + 2 * rb + hb) + 4 * n
+    byts_b = n * H * (2 * rb + hb + rb + (hb if rb != hb else 0)) + 4 * n
+    mf, mb = _time(f, iters), _time(b, iters)
+    return {"op": "add_rms_norm", "N": n, "H": H, "residual": str(res_dtype).replace("torch.", ""), "fwd_ms": mf,
+            "fwd_gbs": byts_f / mf / 1e6, "bwd_ms": mb, "bwd_gbs": byts_b / mb / 1e6}
+
+
+def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "addrmsnorm", "rope", "swiglu"), n=65536):
     out = []
     g = torch.Generator(device=dev).manual_seed(9)
     if "rmsnorm" in ops:
@@ -143,6 +184,11 @@ def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "rope", "swiglu"), n=65
             mf, mb = _time(f, iters), _time(b, iters)
             out.append({"op": "rms_norm", "N": n, "H": H, "fwd_ms": mf, "fwd_gbs": bf / mf / 1e6, "bwd_ms": mb,
                         "bwd_gbs": bb / mb / 1e6})
+    if "addrmsnorm" in ops:
+        for res_dtype in (torch.bfloat16, torch.float32):
+            r = _add_rms_case(dev, g, n, 768, res_dtype, iters, profile)
+            if r is not None:
+                out.append(r)
     if "rope" in ops:
         B, T, D = n // 2048, 2048, 64
         q = torch.randn(B, T, 12, D, device=dev, generator=g).bfloat16().transpose(1, 2)
@@ -349,7 +395,7 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += qkv_cases(dev, iters, profile, n=ce_rows)
     if "torch" in ops and not profile:
         res += torch_comparators(dev, iters, attn_seqs)
-    bw = [o for o in ops if o in ("rmsnorm", "rope", "swiglu")]
+    bw = [o for o in ops if o in ("rmsnorm", "addrmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))
     torch.cuda.synchronize()
@@ -368,7 +414,7 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
 
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ops", default="attention,ce,rmsnorm,rope,swiglu")
+    ap.add_argument("--ops", default="attention,ce,rmsnorm,addrmsnorm,rope,swiglu")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--profile", action="store_true")
     ap.add_argument("--seqs", default="1024,2048,4096")
