@@ -21,7 +21,7 @@ namespace {
 
 constexpr int kWarps = 8;           // rows in flight per block
 constexpr int kChunk = 8;           // elements per lane per chunk
-constexpr int kBwdBlocksPerSM = 3;  // persistent backward grid (3 resident blocks per SM)
+constexpr int kBwdBlocksPerSM = 3;  // persistent backward grid: at most 3 resident blocks per SM
 
 // Load / store 8 consecutive elements as floats (16 or 32 bytes).
 template <typename T>
@@ -136,16 +136,69 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_scalar(const TX* __restri
 //   dn   = dy * w
 //   dx   = rstd * (dn - x * rstd^2 * sum(dn * x) / dim)  (+ g_res if GRES)
 //   dw_p = sum_rows dy * x * rstd                       (per block partial)
-// Only the dW partials live in registers across rows; each row is read twice
-// (dot product, then dx), the second time from L1, so three blocks of eight
-// warps fit per SM and enough rows are in flight to stream at HBM speed.
+// Each warp holds its current row (x, dy and g_res as raw 16-byte words) in
+// registers and issues the loads of its next row before it reduces and writes
+// the current one, so two rows per warp are in flight and the per-row
+// shuffle reduction hides under the next row's load latency.  The dW
+// partials stay in registers across all rows the warp visits.
 // ---------------------------------------------------------------------------
+template <typename T>
+struct Raw8 {  // 8 consecutive elements as raw 16-byte words
+  uint4 q[sizeof(T) / 2];
+};
+
+template <typename T>
+__device__ __forceinline__ void raw_load(Raw8<T>& r, const T* p) {
+  const uint4* s = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < int(sizeof(T) / 2); ++i) r.q[i] = __ldg(s + i);
+}
+
+template <typename T>
+__device__ __forceinline__ void raw_unpack(const Raw8<T>& r, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(r.q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(u[i]);
+  } else {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(r.q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) unpack2<T>(u[i], v[2 * i], v[2 * i + 1]);
+  }
+}
+
+// Sum the 8 warps' dW partials of a block through shared memory and write the
+// block's partial row.
+template <int NC>
+__device__ __forceinline__ void block_partial(const float (&acc)[NC][8], float* red, float* __restrict__ partial,
+                                              int dim) {
+  const int lane = lane_id();
+  const int warp = warp_id();
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 32 + lane) * kChunk;
+    if (col < dim) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red[warp * dim + col + i] = acc[c][i];
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kWarps; ++q) s += red[q * dim + col];
+    partial[int64_t(blockIdx.x) * dim + col] = s;
+  }
+}
+
+// Rows wider than 1024 elements (6 or 8 chunks per lane): only the dW partials
+// stay in registers; each row is read twice (dot product, then dx), the second
+// time from L1.
 template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES, int NC>
-__global__ void __launch_bounds__(kWarps * 32, (NC <= 4 ? 3 : 1))
-    rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rstd,
-                const TG* __restrict__ dy, const TGR* __restrict__ gres, TD* __restrict__ dx,
-                TG* __restrict__ dx2, float* __restrict__ partial, int64_t rows, int dim) {
-  // dx2 (optional): dx once more, rounded to dy's dtype
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    rms_bwd_reread(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rstd,
+                   const TG* __restrict__ dy, const TGR* __restrict__ gres, TD* __restrict__ dx,
+                   TG* __restrict__ dx2, float* __restrict__ partial, int64_t rows, int dim) {
   extern __shared__ float red[];  // [kWarps][dim]
   const int lane = lane_id();
   const int warp = warp_id();
@@ -194,22 +247,99 @@ __global__ void __launch_bounds__(kWarps * 32, (NC <= 4 ? 3 : 1))
       }
     }
   }
-  // block reduction of the dW partials
+  block_partial<NC>(acc, red, partial, dim);
+}
+
+// Rows of at most 1024 elements (1 to 4 chunks per lane): row in registers,
+// next row prefetched.
+template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES, int NC>
+__global__ void __launch_bounds__(kWarps * 32)
+    rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rstd,
+                const TG* __restrict__ dy, const TGR* __restrict__ gres, TD* __restrict__ dx,
+                TG* __restrict__ dx2, float* __restrict__ partial, int64_t rows, int dim) {
+  // dx2 (optional): dx once more, rounded to dy's dtype
+  extern __shared__ float red[];  // [kWarps][dim]
+  const int lane = lane_id();
+  const int warp = warp_id();
+  const int64_t stride = int64_t(gridDim.x) * kWarps;
+  float acc[NC][8];
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int col = (c * 32 + lane) * kChunk;
-    if (col < dim) {
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) red[warp * dim + col + i] = acc[c][i];
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
+
+  Raw8<TX> xc[NC];
+  Raw8<TG> gc[NC];
+  Raw8<TGR> rc[GRES ? NC : 1];
+  float inv_c = 0.f;
+  auto load_row = [&](int64_t row, Raw8<TX>(&xs)[NC], Raw8<TG>(&gs)[NC], Raw8<TGR>(&rs)[GRES ? NC : 1],
+                      float& inv) {
+    inv = __ldg(rstd + row);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * kChunk;
+      if (col < dim) {
+        raw_load<TX>(xs[c], x + row * dim + col);
+        raw_load<TG>(gs[c], dy + row * dim + col);
+        if constexpr (GRES) raw_load<TGR>(rs[c], gres + row * dim + col);
+      }
     }
-  }
-  __syncthreads();
-  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
-    float s = 0.f;
+  };
+
+  int64_t row = int64_t(blockIdx.x) * kWarps + warp;
+  if (row < rows) load_row(row, xc, gc, rc, inv_c);
+  for (; row < rows; row += stride) {
+    Raw8<TX> xn[NC];
+    Raw8<TG> gn[NC];
+    Raw8<TGR> rn[GRES ? NC : 1];
+    float inv_n = 0.f;
+    if (row + stride < rows) load_row(row + stride, xn, gn, rn, inv_n);
+
+    float dot = 0.f;
 #pragma unroll
-    for (int q = 0; q < kWarps; ++q) s += red[q * dim + col];
-    partial[int64_t(blockIdx.x) * dim + col] = s;
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * kChunk;
+      if (col < dim) {
+        float xv[8], gv[8], wv[8];
+        raw_unpack<TX>(xc[c], xv);
+        raw_unpack<TG>(gc[c], gv);
+        load8<TW>(w + col, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot = fmaf(gv[i] * wv[i], xv[i], dot);
+      }
+    }
+    dot = warp_sum(dot);
+    const float inv = inv_c;
+    const float k = inv * inv * dot / float(dim);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * kChunk;
+      if (col < dim) {
+        float xv[8], gv[8], wv[8], o[8];
+        raw_unpack<TX>(xc[c], xv);
+        raw_unpack<TG>(gc[c], gv);
+        load8<TW>(w + col, wv);
+        float rg[8];
+        if constexpr (GRES) raw_unpack<TGR>(rc[c], rg);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[i] = inv * (gv[i] * wv[i] - xv[i] * k);
+          if constexpr (GRES) o[i] += rg[i];
+          acc[c][i] = fmaf(gv[i], xv[i] * inv, acc[c][i]);
+        }
+        store8<TD>(dx + row * dim + col, o);
+        if (dx2 != nullptr) store8<TG>(dx2 + row * dim + col, o);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      xc[c] = xn[c];
+      gc[c] = gn[c];
+      if constexpr (GRES) rc[c] = rn[c];
+    }
+    inv_c = inv_n;
   }
+  block_partial<NC>(acc, red, partial, dim);
 }
 
 template <typename TX, typename TW, typename TG, typename TGR, typename TD, bool GRES>
@@ -348,18 +478,25 @@ int launch_bwd(const void* x, const void* w, const float* rstd, const void* dy, 
       case 2: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2>; break;
       case 3: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3>; break;
       case 4: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4>; break;
-      case 6: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6>; break;
-      default: fn = (const void*)rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8>; break;
+      case 6: fn = (const void*)rms_bwd_reread<TX, TW, TG, TGR, TD, GRES, 6>; break;
+      default: fn = (const void*)rms_bwd_reread<TX, TW, TG, TGR, TD, GRES, 8>; break;
     }
     int st = set_smem_limit(fn, smem);
     if (st != MT_OK) return st;
+    // one wave: as many blocks as are resident at once (the workspace holds 3 per SM)
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kWarps * 32, smem) == cudaSuccess && per_sm > 0 &&
+        per_sm < kBwdBlocksPerSM) {
+      const int cap = get_sm_count() * per_sm;
+      if (nblocks > cap) nblocks = cap;
+    }
     switch (nc) {
       case 1: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 1><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
       case 2: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 2><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
       case 3: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 3><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
       case 4: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 4><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
-      case 6: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 6><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
-      default: rms_bwd_vec<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      case 6: rms_bwd_reread<TX, TW, TG, TGR, TD, GRES, 6><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
+      default: rms_bwd_reread<TX, TW, TG, TGR, TD, GRES, 8><<<nblocks, kWarps * 32, smem, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d); break;
     }
   } else {
     rms_bwd_scalar<TX, TW, TG, TGR, TD, GRES><<<nblocks, kWarps * 32, 0, stream>>>(X, W, rstd, G, GR, DX, DX2, partial, rows, d);
