@@ -8,9 +8,12 @@
 //   (model.py:228-235).
 //
 // B200 design
-//   * One CTA = two consecutive 128-row query tiles ("slots") of one
+//   * Work item = two consecutive 128-row query tiles ("slots") of one
 //     (batch, query head); both slots share one K/V tile stream (3 stages).
-//     One CTA per SM (128 KB smem, all 512 TMEM columns).
+//     Persistent: one CTA per SM (128 KB smem, all 512 TMEM columns) walks
+//     the items with a grid stride, so the next item's Q load and first
+//     S = Q K^T overlap this item's last softmax and epilogue, and barrier
+//     setup and TMEM allocation happen once per SM.
 //   * Warp roles: warps 0-3 / 4-7 = softmax of slot 0 / 1 (thread i owns TMEM
 //     lane = query row i of its slot), warp 8 = TMA producer (+ TMEM
 //     allocation), warp 9 = tcgen05.mma issuer.
@@ -26,7 +29,7 @@
 //     only V is read from shared memory (shared-memory bandwidth, not the
 //     tensor core, limits an all-shared-memory P V at N = D = 64).
 //   * Causal: key tiles 0..qtile only; the diagonal tile is masked in
-//     registers.  CTAs are launched heaviest query tile first.
+//     registers.  Items are ordered heaviest query tile first.
 //   * Every mbarrier wait is bounded (status word + early exit, no trap).
 #include <cmath>
 #include <type_traits>
@@ -70,7 +73,7 @@ struct FwdParams {
   void* o;
   float* lse;
   int64_t os[4];
-  int T, Hq, Hkv, repeats, n_qtiles, n_pairs;
+  int T, Hq, Hkv, repeats, n_qtiles, n_pairs, n_items;
   int ht_swapped;  // tensor-map coordinate order (D, H, T, B) instead of (D, T, H, B)
   float scale_log2;
   uint32_t* status;
@@ -82,6 +85,33 @@ __device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, uint
     tma_load_4d(dst, map, bar, 0, h, t0, b);
   else
     tma_load_4d(dst, map, bar, 0, t0, h, b);
+}
+
+// Item order: one (batch, kv head) after another; inside it the query-tile
+// pairs go heaviest first, and the `repeats` query heads of one pair are
+// adjacent.  The items resident at one time then share a few kv heads, so
+// their K/V tiles come from DRAM about once.
+struct FwdItem {
+  int b, hk, h, pair;
+  int nkv0, nkv1, n_kv;  // key tiles seen by slot 0, slot 1 (0: no slot 1) and the item
+};
+
+__device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int it) {
+  FwdItem w;
+  const int per_kv = p.n_pairs * p.repeats;
+  const int bk = it / per_kv;
+  const int rem = it - bk * per_kv;
+  const int pi = rem / p.repeats;
+  w.b = bk / p.Hkv;
+  w.hk = bk - w.b * p.Hkv;
+  w.h = w.hk * p.repeats + (rem - pi * p.repeats);
+  w.pair = p.n_pairs - 1 - pi;  // heaviest pair first
+  // slot s handles query tile 2*pair + s; it sees key tiles 0..(2*pair + s)
+  const bool active1 = (2 * w.pair + 1) < p.n_qtiles;
+  w.nkv0 = 2 * w.pair + 1;
+  w.nkv1 = active1 ? 2 * w.pair + 2 : 0;
+  w.n_kv = active1 ? w.nkv1 : w.nkv0;
+  return w;
 }
 
 template <typename T, int D>
@@ -106,30 +136,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bar_s_free = bar_s_full + kSlots;    // [kSlots]
   uint64_t* bar_p_full = bar_s_free + kSlots;    // [kSlots]
   uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots] (+kSlots: final MMA drains)
+  uint64_t* bar_q_free = bar_o_done + 2 * kSlots;  // [kSlots]: last S of an item read its Q tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
 
-  // Launch order: one (batch, kv head) after another; inside it the query-tile
-  // pairs go heaviest first, and the `repeats` query heads of one pair are
-  // adjacent.  Every CTA that streams a kv head's K/V tiles is then resident
-  // at about the same time, so those tiles come from DRAM about once.
-  const int per_kv = p.n_pairs * p.repeats;
-  const int bk = (int)blockIdx.x / per_kv;
-  const int rem = (int)blockIdx.x - bk * per_kv;
-  const int pi = rem / p.repeats;
-  const int b = bk / p.Hkv;
-  const int hk = bk - b * p.Hkv;
-  const int h = hk * p.repeats + (rem - pi * p.repeats);
-  const int pair = p.n_pairs - 1 - pi;  // heaviest pair first
-  // slot s handles query tile 2*pair + s; it sees key tiles 0..(2*pair + s)
-  const bool active1 = (2 * pair + 1) < p.n_qtiles;
-  const int nkv0 = 2 * pair + 1;
-  const int nkv1 = active1 ? 2 * pair + 2 : 0;
-  const int n_kv = active1 ? nkv1 : nkv0;
-
+  // Every K/V stage is released by two arrivals, one per slot: a commit after
+  // the slot's P V read it, or a plain arrival from a slot that does not read
+  // that tile (slot 0 on its item's last tile, slot 1 of an item without a
+  // second query tile) once the tile's load has been issued.
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&bar_q[s], 1);
+      mbar_init(&bar_q_free[s], 1);
       mbar_init(&bar_s_full[s], 1);
       mbar_init(&bar_s_free[s], 128);
       mbar_init(&bar_p_full[s], 128);
@@ -140,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&bar_k_full[s], 1);
       mbar_init(&bar_v_full[s], 1);
-      mbar_init(&bar_kv_empty[s], active1 ? 2 : 1);
+      mbar_init(&bar_kv_empty[s], kSlots);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -154,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{p.status, abort_flag, kKernelId};
+  const int first = (int)blockIdx.x, stride = (int)gridDim.x;
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -161,24 +180,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_k);
       tma_prefetch_desc(&p.tm_v);
-      for (int s = 0; s < (active1 ? 2 : 1); ++s) {
-        mbar_arrive_expect_tx(&bar_q[s], C::TILE);
-        tma_tile(sQ + s * C::TILE, &p.tm_q, &bar_q[s], (2 * pair + s) * kBM, h, b, p.ht_swapped);
-      }
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::NST;
-        if (j >= C::NST && !wait_bounded(wc, &bar_kv_empty[st], ((j / C::NST) & 1) ^ 1, 1)) break;
-        mbar_arrive_expect_tx(&bar_k_full[st], C::TILE);
-        tma_tile(sK + st * C::TILE, &p.tm_k, &bar_k_full[st], j * kBN, hk, b, p.ht_swapped);
-        mbar_arrive_expect_tx(&bar_v_full[st], C::TILE);
-        tma_tile(sV + st * C::TILE, &p.tm_v, &bar_v_full[st], j * kBN, hk, b, p.ht_swapped);
-        ++issued;
+      int g = 0;             // K/V tiles issued by this CTA
+      int nq[kSlots] = {0, 0};  // Q tiles issued per slot
+      bool ok = true;
+      for (int it = first; ok && it < p.n_items; it += stride) {
+        const FwdItem w = fwd_item(p, it);
+        for (int s = 0; s < (w.nkv1 > 0 ? 2 : 1); ++s) {
+          if (nq[s] > 0 && !wait_bounded(wc, &bar_q_free[s], (nq[s] - 1) & 1, 14)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar_q[s], C::TILE);
+          tma_tile(sQ + s * C::TILE, &p.tm_q, &bar_q[s], (2 * w.pair + s) * kBM, w.h, w.b, p.ht_swapped);
+          ++nq[s];
+        }
+        for (int j = 0; ok && j < w.n_kv; ++j, ++g) {
+          const int st = g % C::NST;
+          if (g >= C::NST && !wait_bounded(wc, &bar_kv_empty[st], ((g / C::NST) & 1) ^ 1, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar_k_full[st], C::TILE);
+          tma_tile(sK + st * C::TILE, &p.tm_k, &bar_k_full[st], j * kBN, w.hk, w.b, p.ht_swapped);
+          mbar_arrive_expect_tx(&bar_v_full[st], C::TILE);
+          tma_tile(sV + st * C::TILE, &p.tm_v, &bar_v_full[st], j * kBN, w.hk, w.b, p.ht_swapped);
+        }
       }
       if (*abort_flag) {
         // copies already issued must land before shared memory is released
-        for (int s = 0; s < (active1 ? 2 : 1); ++s) wait_drain(wc, &bar_q[s], 0, 11);
-        for (int j = (issued > C::NST ? issued - C::NST : 0); j < issued; ++j) {
+        for (int s = 0; s < kSlots; ++s)
+          if (nq[s] > 0) wait_drain(wc, &bar_q[s], (nq[s] - 1) & 1, 11);
+        for (int j = (g > C::NST ? g - C::NST : 0); j < g; ++j) {
           wait_drain(wc, &bar_k_full[j % C::NST], (j / C::NST) & 1, 12);
           wait_drain(wc, &bar_v_full[j % C::NST], (j / C::NST) & 1, 12);
         }
@@ -214,30 +246,64 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       // that slot has read S(j), and its P V(j) as soon as it has written
       // P(j), whatever the other slot is doing.
       const int slot = warp - 9;
-      const int nkv = slot ? nkv1 : nkv0;
-      bool ok = nkv > 0 && wait_bounded(wc, &bar_q[slot], 0, 2) && wait_bounded(wc, &bar_k_full[0], 0, 3);
-      if (ok) {
-        tc_fence_after();
-        issue_s(slot, 0);
-        umma_commit(&bar_s_full[slot]);
-      }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j % C::NST;
-        if (j + 1 < nkv) {
-          const int st1 = (j + 1) % C::NST;
-          if (!wait_bounded(wc, &bar_k_full[st1], ((j + 1) / C::NST) & 1, 4) ||
-              !wait_bounded(wc, &bar_s_free[slot], j & 1, 5))
-            break;
-          tc_fence_after();
-          issue_s(slot, st1);
-          umma_commit(&bar_s_full[slot]);
+      int g = 0;   // K/V tiles of the CTA's items so far
+      int cs = 0;  // S products issued
+      int cp = 0;  // P V products issued
+      int nq = 0;  // Q tiles used
+      bool ok = true;
+      for (int it = first; ok && it < p.n_items; it += stride) {
+        const FwdItem w = fwd_item(p, it);
+        const int nkv = slot ? w.nkv1 : w.nkv0;
+        if (nkv > 0) {
+          ok = wait_bounded(wc, &bar_q[slot], nq & 1, 2) &&
+               wait_bounded(wc, &bar_k_full[g % C::NST], (g / C::NST) & 1, 3) &&
+               (cs == 0 || wait_bounded(wc, &bar_s_free[slot], (cs - 1) & 1, 5));
+          if (ok) {
+            tc_fence_after();
+            issue_s(slot, g % C::NST);
+            umma_commit(&bar_s_full[slot]);
+            ++cs;
+            if (nkv == 1) umma_commit(&bar_q_free[slot]);
+          }
+          for (int j = 0; ok && j < nkv; ++j) {
+            const int gj = g + j;
+            const int st = gj % C::NST;
+            if (j + 1 < nkv) {
+              const int g1 = gj + 1;
+              if (!wait_bounded(wc, &bar_k_full[g1 % C::NST], (g1 / C::NST) & 1, 4) ||
+                  !wait_bounded(wc, &bar_s_free[slot], (cs - 1) & 1, 5)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(slot, g1 % C::NST);
+              umma_commit(&bar_s_full[slot]);
+              ++cs;
+              if (j + 2 == nkv) umma_commit(&bar_q_free[slot]);  // the item's last S has been issued
+            }
+            if (!wait_bounded(wc, &bar_v_full[st], (gj / C::NST) & 1, 7) ||
+                !wait_bounded(wc, &bar_p_full[slot], cp & 1, 6)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(slot, st, j > 0);
+            umma_commit(&bar_o_done[slot]);
+            umma_commit(&bar_kv_empty[st]);  // this slot's release of the stage
+            ++cp;
+          }
+          ++nq;
         }
-        if (!wait_bounded(wc, &bar_v_full[st], (j / C::NST) & 1, 7) || !wait_bounded(wc, &bar_p_full[slot], j & 1, 6))
-          break;
-        tc_fence_after();
-        issue_pv(slot, st, j > 0);
-        umma_commit(&bar_o_done[slot]);
-        umma_commit(&bar_kv_empty[st]);  // one arrival per slot that reads this stage
+        // tiles of the item this slot does not read: release them once loaded
+        for (int j = nkv; ok && j < w.n_kv; ++j) {
+          const int gj = g + j;
+          if (!wait_bounded(wc, &bar_v_full[gj % C::NST], (gj / C::NST) & 1, 15)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive(&bar_kv_empty[gj % C::NST]);
+        }
+        g += w.n_kv;
       }
       // every issued MMA completes before TMEM is released (also on abort)
       uint64_t* bar_fin = bar_o_done + kSlots + slot;
@@ -248,111 +314,128 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // ------------------------------------------------------------ softmax
     const int slot = warp >> 2;
     const int r = threadIdx.x & 127;  // query row within the tile == TMEM lane
-    const int qt = 2 * pair + slot;
-    const int nkv = slot ? nkv1 : nkv0;
-    const int qrow = qt * kBM + r;
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + slot * 256 + lane_off;
     const uint32_t tO = tS + C::T_O;
     const uint32_t tP = tS + C::T_P;
-    float m = -INFINITY;
-    float l = 0.f;
-    bool ok = nkv > 0;
-    for (int j = 0; j < nkv; ++j) {
-      if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_s_full[slot], j & 1, 8))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sv[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]);
-        tmem_ld32(tS + c * 32, chunk);
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&bar_s_free[slot]);
-
-      // Row max of the raw scores in 8 independent chains (three-input max:
-      // two new scores per instruction); the causal mask only exists on the
-      // diagonal tile (warp-uniform branch).
-      const bool diag = (j == nkv - 1);
-      if (diag) {
-        const int lim = qrow - j * kBN;  // keys 0..lim of this tile are visible
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (c > lim) sv[c] = __float_as_uint(-INFINITY);
-      }
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sv[i]);
-#pragma unroll
-      for (int c = 8; c < kBN; c += 16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], __uint_as_float(sv[c + i]), __uint_as_float(sv[c + 8 + i]));
-      }
-      const float mx2 = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
-                        p.scale_log2;
-      // Lazy rescaling: the running reference max m (log2 units) only moves
-      // when the tile max exceeds it by more than 8, so P <= 2^8 and O is
-      // rescaled only on those (rare after the first tiles) occasions.
-      float alpha = 1.f;
-      if (mx2 > m + 8.f) {
-        alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mx2);
-        m = mx2;
-      }
-      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-      const float2 nm2 = make_float2(-m, -m);
-
-      // P = exp2(s * scale_log2 - m) rounded to T and packed two per word, all
-      // in registers: this does not touch the P tile, so it overlaps the P V
-      // product of the previous tile.
-      uint32_t pk[kBN / 2];
-      float2 sum4[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float2 x = fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
-        const float2 e = ((c >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-        sum4[(c >> 1) & 3] = add2(sum4[(c >> 1) & 3], e);
-        pk[c >> 1] = pack2<T>(e.x, e.y);
-      }
-      const float2 s01 = add2(add2(sum4[0], sum4[1]), add2(sum4[2], sum4[3]));
-      l = l * alpha + (s01.x + s01.y);
-
-      if (j > 0) {
-        // P V of the previous tile must be finished before the P tile is
-        // overwritten and O is rescaled.
-        if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (j - 1) & 1, 9))) {
+    int cs = 0;  // S tiles read
+    int cp = 0;  // P tiles written
+    bool ok = true;
+    for (int it = first; ok && it < p.n_items; it += stride) {
+      const FwdItem w = fwd_item(p, it);
+      const int nkv = slot ? w.nkv1 : w.nkv0;
+      if (nkv == 0) continue;
+      const int qt = 2 * w.pair + slot;
+      const int qrow = qt * kBM + r;
+      float m = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_s_full[slot], cs & 1, 8))) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
+        uint32_t sv[kBN];
 #pragma unroll
-      for (int ch = 0; ch < kBN / 32; ++ch) tmem_st16(tP + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[ch * 16]));
-      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
-#pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t ov[16];
-          tmem_ld16(tO + c * 16, ov);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st16(tO + c * 16, ov);
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]);
+          tmem_ld32(tS + c * 32, chunk);
         }
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&bar_s_free[slot]);
+        ++cs;
+
+        // Row max of the raw scores in 8 independent chains (three-input max:
+        // two new scores per instruction); the causal mask only exists on the
+        // diagonal tile (warp-uniform branch).
+        const bool diag = (j == nkv - 1);
+        if (diag) {
+          const int lim = qrow - j * kBN;  // keys 0..lim of this tile are visible
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c > lim) sv[c] = __float_as_uint(-INFINITY);
+        }
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sv[i]);
+#pragma unroll
+        for (int c = 8; c < kBN; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            mx8[i] = fmax3(mx8[i], __uint_as_float(sv[c + i]), __uint_as_float(sv[c + 8 + i]));
+        }
+        const float mx2 =
+            fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
+            p.scale_log2;
+        // Lazy rescaling: the running reference max m (log2 units) only moves
+        // when the tile max exceeds it by more than 8, so P <= 2^8 and O is
+        // rescaled only on those (rare after the first tiles) occasions.
+        float alpha = 1.f;
+        if (mx2 > m + 8.f) {
+          alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mx2);
+          m = mx2;
+        }
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nm2 = make_float2(-m, -m);
+
+        // P = exp2(s * scale_log2 - m) rounded to T and packed two per word, all
+        // in registers: this does not touch the P tile, so it overlaps the P V
+        // product of the previous tile.
+        uint32_t pk[kBN / 2];
+        float2 sum4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          const float2 x = fma2(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+          const float2 e =
+              ((c >> 1) & 7) < kPolyPairs ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          sum4[(c >> 1) & 3] = add2(sum4[(c >> 1) & 3], e);
+          pk[c >> 1] = pack2<T>(e.x, e.y);
+        }
+        const float2 s01 = add2(add2(sum4[0], sum4[1]), add2(sum4[2], sum4[3]));
+        l = l * alpha + (s01.x + s01.y);
+
+        if (j > 0) {
+          // P V of the previous tile must be finished before the P tile is
+          // overwritten and O is rescaled.  (Before an item's first tile the
+          // previous item's epilogue has already waited for its last P V.)
+          if (!__all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (cp - 1) & 1, 9))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int ch = 0; ch < kBN / 32; ++ch)
+          tmem_st16(tP + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[ch * 16]));
+        if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t ov[16];
+            tmem_ld16(tO + c * 16, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st16(tO + c * 16, ov);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bar_p_full[slot]);
+        ++cp;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bar_p_full[slot]);
-    }
-    // epilogue: O / l -> global, logsumexp (natural log of scaled scores)
-    if (ok && __all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (nkv - 1) & 1, 10))) {
+      // epilogue: O / l -> global, logsumexp (natural log of scaled scores).
+      // O is read completely before this slot's next P tile is announced, so
+      // the next item's first P V (which overwrites O) cannot overtake it.
+      if (!ok || !__all_sync(0xffffffffu, wait_bounded(wc, &bar_o_done[slot], (cp - 1) & 1, 10))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float inv_l = 1.f / l;
-      T* orow = static_cast<T*>(p.o) + int64_t(b) * p.os[0] + int64_t(h) * p.os[1] + int64_t(qrow) * p.os[2];
+      T* orow = static_cast<T*>(p.o) + int64_t(w.b) * p.os[0] + int64_t(w.h) * p.os[1] + int64_t(qrow) * p.os[2];
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {
         uint32_t ov[16];
@@ -372,8 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           *reinterpret_cast<uint4*>(orow + c * 16 + 8) = w1;
         }
       }
+      tc_fence_before();
       if (qrow < p.T)
-        p.lse[(int64_t(b) * p.Hq + h) * p.T + qrow] = (m + __log2f(l)) * 0.69314718055994530942f;
+        p.lse[(int64_t(w.b) * p.Hq + w.h) * p.T + qrow] = (m + __log2f(l)) * 0.69314718055994530942f;
     }
   }
 
@@ -392,8 +476,8 @@ int launch_fwd(const FwdParams& prm, int B, int Hq, cudaStream_t stream) {
   auto kern = attn_fwd_kernel<T, D>;
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
-  const int64_t blocks = int64_t(B) * Hq * prm.n_pairs;
-  if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+  // persistent: one CTA per SM (the kernel's shared memory and TMEM allow one)
+  const int blocks = prm.n_items < get_sm_count() ? prm.n_items : get_sm_count();
   record_timing_event(0, stream);
   kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
   record_timing_event(1, stream);
@@ -482,6 +566,8 @@ extern "C" int mt_attention_fwd(const void* q, const void* k, const void* v, voi
   prm.repeats = (int)(Hq / Hkv);
   prm.n_qtiles = (int)((T + kBM - 1) / kBM);
   prm.n_pairs = (prm.n_qtiles + 1) / 2;
+  if (B * Hq * prm.n_pairs > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+  prm.n_items = (int)(B * Hq * prm.n_pairs);
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.status = status;
   if (prm.n_qtiles > 65535) return MT_ERR_INVALID_ARGUMENT;
