@@ -198,16 +198,25 @@ MT_API int mt_swiglu_packed_bwd(const void* gu, const void* dy, void* dgu, int d
  * 8 elements), D in {32, 64}, dtype bf16 or fp16.
  * lse: [B, Hq, T] fp32 contiguous (natural-log logsumexp of scaled scores).
  * scale: softmax scale (1/sqrt(D) in the reference).
+ * workspace: device scratch of mt_attention_fwd_workspace_bytes() bytes.
  * status: device uint32 (see above).
  * ------------------------------------------------------------------- */
 MT_API int mt_attention_fwd(const void* q, const void* k, const void* v, void* o,
                      float* lse, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
                      int64_t T, int64_t D, const int64_t* qs, const int64_t* ks,
                      const int64_t* vs, const int64_t* os, float scale,
+                     void* workspace, int64_t workspace_bytes,
                      uint32_t* status, void* stream);
 
-/* Workspace for the backward: fp32 delta [B*Hq*Tp] and fp32 dQ accumulator
- * [B*Hq*Tp*D], Tp = T rounded up to 128. */
+/* Workspace for the forward (16-byte aligned): the persistent kernel's work
+ * counter, zeroed on the stream by every call.  One call at a time per
+ * workspace. */
+MT_API int64_t mt_attention_fwd_workspace_bytes(int64_t B, int64_t Hq, int64_t T,
+                                                int64_t D);
+
+/* Workspace for the backward: fp32 delta and -lse*log2(e) [B*Hq*Tp], fp32 dQ
+ * accumulator [B*Hq*Tp*D] and the persistent kernel's work counter,
+ * Tp = T rounded up to 128. */
 MT_API int64_t mt_attention_bwd_workspace_bytes(int64_t B, int64_t Hq, int64_t T,
                                          int64_t D);
 

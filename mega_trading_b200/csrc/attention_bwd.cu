@@ -11,10 +11,16 @@
 //   * preprocess kernel: Delta = rowsum(O * dO) and lse * log2(e) into padded
 //     fp32 workspace rows (+inf past T so padded queries get P = 0); the fp32
 //     dQ accumulator is zeroed with cudaMemsetAsync.
-//   * main kernel: one CTA = one 128-key tile of one (batch, KV head).  It
+//   * main kernel: work item = one 128-key tile of one (batch, KV head).  It
 //     loops over every query head of the GQA group and every causal query
-//     tile (query tile >= key tile).  All five products are tcgen05.mma with
-//     fp32 accumulators in TMEM:
+//     tile (query tile >= key tile).  Persistent: one CTA per SM takes items
+//     from a global work counter (zeroed by the preprocess kernel; the
+//     producer warp fetches each item and passes it to the MMA and compute
+//     warps through a shared-memory ring), so the CTAs stay balanced although
+//     items differ 16x in work; the next item's first Q/dO tiles are
+//     prefetched and its K/V load overlaps this item's last dQ drain and
+//     dK/dV epilogue.  All five products are tcgen05.mma with fp32
+//     accumulators in TMEM:
 //         S^T  = K Q^T        cols [0,128)        (M=128 keys, N=128 queries)
 //         dP^T = V dO^T       cols [128,256)
 //         dV  += P^T dO       cols [256,256+D)    (accumulated over the group)
@@ -50,6 +56,7 @@ constexpr int kBK = 128;  // keys per CTA
 constexpr int kBQ = 128;  // queries per tile
 constexpr int kNQ = 3;    // Q/dO pipeline stages (loads run ~2 tiles ahead of the MMAs)
 constexpr int kThreads = 320;
+constexpr int kRing = 4;  // work items announced ahead by the producer warp
 constexpr uint32_t kKernelId = 2;
 
 template <int D>
@@ -85,7 +92,9 @@ struct BwdParams {
   int64_t dks[4], dvs[4];
   int T, Tp, Hq, Hkv, repeats, n_tiles;
   int n_heads;  // B * Hkv
-  int group;    // (batch, kv head) pairs whose key tiles are interleaved in launch order
+  int group;    // (batch, kv head) pairs whose key tiles are interleaved in item order
+  int n_items;  // n_heads * n_tiles
+  int* sched;   // work counter (next item), zero at launch
   // optional RoPE tables [T, D/2] (row stride rope_ld): dk is rotated back by
   // -theta(key) before rounding, giving the gradient of the un-rotated keys
   const void* rope_cos;
@@ -146,6 +155,31 @@ __device__ __forceinline__ void store_row32(uint8_t* tile, int row, int col0, co
   }
 }
 
+// Item order: groups of `group` (batch, kv head) pairs; inside a group the
+// key tiles go heaviest (smallest index) first, cycling over the group's
+// heads.  The items resident at one time then share a few heads' Q / dO tiles
+// and fp32 dQ rows in L2 instead of streaming every head's.
+struct BwdItem {
+  int b, hk, kt;
+  int n_q, n_it;  // causal query tiles per head (kt .. n_tiles-1); iterations (x repeats)
+};
+
+__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int it) {
+  BwdItem w;
+  const int per_group = p.group * p.n_tiles;
+  const int grp = it / per_group;
+  const int rem = it - grp * per_group;
+  const int g0 = grp * p.group;
+  const int gsz = min(p.group, p.n_heads - g0);
+  w.kt = rem / gsz;
+  const int bk = g0 + (rem - w.kt * gsz);
+  w.b = bk / p.Hkv;
+  w.hk = bk - w.b * p.Hkv;
+  w.n_q = p.n_tiles - w.kt;
+  w.n_it = w.n_q * p.repeats;
+  return w;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
@@ -175,24 +209,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
   uint64_t* bar_dq_free = bar_sd_full + 4;
   uint64_t* bar_done = bar_sd_full + 5;
   uint64_t* bar_pt_free = bar_sd_full + 6;  // dV of the previous tile done: P^T TMEM free
+  uint64_t* bar_item = bar_sd_full + 7;     // an item's last dQ done: its K/V, dK and dV are free
+  uint64_t* ring_full = bar_sd_full + 8;    // [kRing] item id published
+  uint64_t* ring_empty = ring_full + kRing;  // [kRing] item id read by the 9 consumer warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
-
-  // Launch order: groups of `group` (batch, kv head) pairs; inside a group the
-  // key tiles go heaviest (smallest index) first, cycling over the group's
-  // heads.  The CTAs resident at one time then share a few heads' Q / dO
-  // tiles and fp32 dQ rows in L2 instead of streaming every head's.
-  const int per_group = p.group * p.n_tiles;
-  const int grp = (int)blockIdx.x / per_group;
-  const int rem = (int)blockIdx.x - grp * per_group;
-  const int g0 = grp * p.group;
-  const int gsz = min(p.group, p.n_heads - g0);
-  const int kt = rem / gsz;
-  const int bk = g0 + (rem - kt * gsz);
-  const int b = bk / p.Hkv;
-  const int hk = bk - b * p.Hkv;
-  const int n_q = p.n_tiles - kt;  // causal query tiles per head: kt .. n_tiles-1
-  const int n_it = n_q * p.repeats;
+  volatile int* ring_ids = reinterpret_cast<volatile int*>(bars + 26);  // [kRing]
 
   if (threadIdx.x == 0) {
     mbar_init(bar_kv, 1);
@@ -207,6 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
     mbar_init(bar_dq_free, 256);
     mbar_init(bar_done, 1);
     mbar_init(bar_pt_free, 1);
+    mbar_init(bar_item, 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&ring_full[s], 1);
+      mbar_init(&ring_empty[s], 9);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -219,6 +246,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{p.status, abort_flag, kKernelId};
+  // k-th item of this CTA (consumers): wait for the producer's announcement,
+  // release the ring entry; -1 = no more work or abort
+  auto next_item = [&](int k, bool whole_warp) -> int {
+    const int slot = k % kRing;
+    const bool got = wait_bounded(wc, &ring_full[slot], (k / kRing) & 1, 18);
+    const int it = got ? ring_ids[slot] : -1;
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || lane == 0) mbar_arrive(&ring_empty[slot]);
+    return it;
+  };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -227,29 +264,54 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       tma_prefetch_desc(&p.tm_k);
       tma_prefetch_desc(&p.tm_v);
       tma_prefetch_desc(&p.tm_do);
-      mbar_arrive_expect_tx(bar_kv, 2 * C::TILE);
-      tma_tile(sK, &p.tm_k, bar_kv, kt * kBK, hk, b, p.sw_k);
-      tma_tile(sV, &p.tm_v, bar_kv, kt * kBK, hk, b, p.sw_v);
-      int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int st = it % kNQ;
-        const int r = it / n_q;
-        const int qi = kt + (it - r * n_q);
-        const int h = hk * p.repeats + r;
-        if (it >= kNQ && !wait_bounded(wc, &bar_q_empty[st], ((it / kNQ) & 1) ^ 1, 1)) break;
+      int ci = 0;   // Q/dO ring tiles issued
+      int nkv = 0;  // K/V tiles issued (one per item)
+      bool ok = true;
+      // ring tile of item-local iteration j: query head r, query tile qi
+      auto issue_ring = [&](const BwdItem& w, int j) -> bool {
+        const int st = ci % kNQ;
+        if (ci >= kNQ && !wait_bounded(wc, &bar_q_empty[st], ((ci / kNQ) & 1) ^ 1, 1)) return false;
+        const int r = j / w.n_q;
+        const int qi = w.kt + (j - r * w.n_q);
+        const int h = w.hk * p.repeats + r;
         mbar_arrive_expect_tx(&bar_q_full[st], 2 * C::TILE + 2 * 512);
-        tma_tile(sQ + st * C::TILE, &p.tm_q, &bar_q_full[st], qi * kBQ, h, b, p.sw_q);
-        tma_tile(sDO + st * C::TILE, &p.tm_do, &bar_q_full[st], qi * kBQ, h, b, p.sw_do);
-        const int64_t row0 = (int64_t(b) * p.Hq + h) * p.Tp + int64_t(qi) * kBQ;
+        tma_tile(sQ + st * C::TILE, &p.tm_q, &bar_q_full[st], qi * kBQ, h, w.b, p.sw_q);
+        tma_tile(sDO + st * C::TILE, &p.tm_do, &bar_q_full[st], qi * kBQ, h, w.b, p.sw_do);
+        const int64_t row0 = (int64_t(w.b) * p.Hq + h) * p.Tp + int64_t(qi) * kBQ;
         bulk_load(sLse + st * 128, p.lse2 + row0, 512, &bar_q_full[st]);
         bulk_load(sDelta + st * 128, p.delta + row0, 512, &bar_q_full[st]);
-        ++issued;
+        ++ci;
+        return true;
+      };
+      for (int k = 0; ok; ++k) {
+        // take the next item from the work counter and announce it
+        const int slot = k % kRing;
+        if (k >= kRing && !wait_bounded(wc, &ring_empty[slot], ((k / kRing) & 1) ^ 1, 17)) break;
+        int it = atomicAdd(p.sched, 1);
+        if (it >= p.n_items) it = -1;
+        ring_ids[slot] = it;
+        mbar_arrive(&ring_full[slot]);
+        if (it < 0) break;
+        const BwdItem w = bwd_item(p, it);
+        // after the first item: the ring runs ahead into this item while the
+        // previous one finishes; K/V are replaced once its last dQ is done
+        const int pre = nkv > 0 ? min(kNQ, w.n_it) : 0;
+        for (int j = 0; ok && j < pre; ++j) ok = issue_ring(w, j);
+        if (!ok || (nkv > 0 && !wait_bounded(wc, bar_item, (nkv - 1) & 1, 14))) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(bar_kv, 2 * C::TILE);
+        tma_tile(sK, &p.tm_k, bar_kv, w.kt * kBK, w.hk, w.b, p.sw_k);
+        tma_tile(sV, &p.tm_v, bar_kv, w.kt * kBK, w.hk, w.b, p.sw_v);
+        ++nkv;
+        for (int j = pre; ok && j < w.n_it; ++j) ok = issue_ring(w, j);
       }
       if (*abort_flag) {
         // copies already issued must land before shared memory is released
-        wait_drain(wc, bar_kv, 0, 11);
-        for (int it = (issued > kNQ ? issued - kNQ : 0); it < issued; ++it)
-          wait_drain(wc, &bar_q_full[it % kNQ], (it / kNQ) & 1, 12);
+        if (nkv > 0) wait_drain(wc, bar_kv, (nkv - 1) & 1, 11);
+        for (int i = (ci > kNQ ? ci - kNQ : 0); i < ci; ++i)
+          wait_drain(wc, &bar_q_full[i % kNQ], (i / kNQ) & 1, 12);
       }
     }
   } else if (warp == 9) {
@@ -279,78 +341,89 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       // Issue order per tile i: S/dP of tile i+1 as soon as the compute warps
       // have read S/dP of tile i, then dV, dK, dQ of tile i -- so the compute
       // warps' softmax of tile i+1 overlaps the three accumulating products.
-      bool ok = wait_bounded(wc, bar_kv, 0, 2) && wait_bounded(wc, &bar_q_full[0], 0, 3);
-      if (ok) {
-        tc_fence_after();
-        issue_sdp(0);
-      }
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int st = it % kNQ;
-        if (!wait_bounded(wc, bar_sd_free, it & 1, 4)) {
-          ok = false;
-          break;
+      // Counters run across items (ci: iterations, n: items).
+      int ci = 0, n = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k, ++n) {
+        const int it = next_item(k, false);
+        if (it < 0) break;
+        const BwdItem w = bwd_item(p, it);
+        // S/dP of the item's first tile: the previous item's last S/dP was
+        // read (waited in its last iteration) and this item's K/V landed
+        ok = wait_bounded(wc, bar_kv, n & 1, 2) && wait_bounded(wc, &bar_q_full[ci % kNQ], (ci / kNQ) & 1, 3);
+        if (ok) {
+          tc_fence_after();
+          issue_sdp(ci % kNQ);
         }
-        if (it + 1 < n_it) {
-          const int st1 = (it + 1) % kNQ;
-          if (!wait_bounded(wc, &bar_q_full[st1], ((it + 1) / kNQ) & 1, 3)) {
+        for (int j = 0; ok && j < w.n_it; ++j, ++ci) {
+          const int st = ci % kNQ;
+          if (!wait_bounded(wc, bar_sd_free, ci & 1, 4)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < w.n_it) {
+            const int c1 = ci + 1;
+            if (!wait_bounded(wc, &bar_q_full[c1 % kNQ], (c1 / kNQ) & 1, 3)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_sdp(c1 % kNQ);
+          }
+          if (!wait_bounded(wc, bar_pds_full, ci & 1, 5)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_sdp(st1);
-        }
-        if (!wait_bounded(wc, bar_pds_full, it & 1, 5)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
-        // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
+          const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
+          // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
 #pragma unroll
-        for (int kk = 0; kk < kBQ / 16; ++kk) {
-          const uint32_t b_off = kk * 16 * C::ROW_BYTES;
-          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),
-                  idesc_acc, acc);
-        }
-        umma_commit(bar_pt_free);
+          for (int kk = 0; kk < kBQ / 16; ++kk) {
+            const uint32_t b_off = kk * 16 * C::ROW_BYTES;
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),
+                    idesc_acc, acc);
+          }
+          umma_commit(bar_pt_free);
 #pragma unroll
-        for (int kk = 0; kk < kBQ / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          const uint32_t b_off = kk * 16 * C::ROW_BYTES;
-          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
-                  make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
-        }
-        umma_commit(&bar_q_empty[st]);  // Q/dO of this stage are no longer read (dQ reads K and dS)
-        if (it > 0 && !wait_bounded(wc, bar_dq_free, (it - 1) & 1, 6)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // dQ = dS K   (M = 128 queries, K = 128 keys in steps of 16)
+          for (int kk = 0; kk < kBQ / 16; ++kk) {
+            const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+            const uint32_t b_off = kk * 16 * C::ROW_BYTES;
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
+                    make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
+          }
+          umma_commit(&bar_q_empty[st]);  // Q/dO of this stage are no longer read (dQ reads K and dS)
+          if (ci > 0 && !wait_bounded(wc, bar_dq_free, (ci - 1) & 1, 6)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // dQ = dS K   (M = 128 queries, K = 128 keys in steps of 16)
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          umma_ss(tmem + C::T_DQ, make_sdesc(ds_base + kk * 2048, 128 * 128, 1024, kSwizzle128),
-                  make_sdesc(k_base + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT), idesc_dq,
-                  kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_ss(tmem + C::T_DQ, make_sdesc(ds_base + kk * 2048, 128 * 128, 1024, kSwizzle128),
+                    make_sdesc(k_base + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT), idesc_dq,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar_dq_full);
+          if (j + 1 == w.n_it) umma_commit(bar_item);
         }
-        umma_commit(bar_dq_full);
       }
       // every issued MMA completes before TMEM is released (also on abort)
       umma_commit(bar_done);
-      if (!ok) wait_drain(wc, bar_done, 0, 13);
+      wait_drain(wc, bar_done, 0, 13);
     }
   } else {
     // ------------------------------------------------------------ compute
     const int wg = warp >> 2;          // query-column half handled by this warpgroup
     const int r = threadIdx.x & 127;   // TMEM lane: key row (S/dP) or query row (dQ)
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
-    const int key = kt * kBK + r;
     bool ok = true;
-    // Drain dQ of tile `pit` (query head ph, query tile pq): TMEM -> swizzled
-    // fp32 staging -> TMA reduce-add into the accumulator.  Returns false on abort.
-    auto drain_dq = [&](int pit, int ph, int pq) -> bool {
+    // Drain dQ of global iteration `pit` (batch pb, query head ph, query tile
+    // pq): TMEM -> swizzled fp32 staging -> TMA reduce-add into the
+    // accumulator.  Returns false on abort.
+    auto drain_dq = [&](int pit, int pb, int ph, int pq) -> bool {
       if (!bar_all(wait_bounded(wc, bar_dq_full, pit & 1, 9), 4, 256)) return false;
       tc_fence_after();
       constexpr int kCols = D / 2;  // dQ columns per warpgroup
@@ -391,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       tc_fence_before();
       mbar_arrive(bar_dq_free);
       fence_proxy_async_smem();
-      const int row0 = (b * p.Hq + ph) * p.Tp + pq * kBQ;
+      const int row0 = (pb * p.Hq + ph) * p.Tp + pq * kBQ;
       if constexpr (kCols == 32) {
         named_bar_sync(1 + wg, 128);
         if (leader) {
@@ -410,150 +483,170 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       }
       return true;
     };
-    int prev_h = 0, prev_q = 0;
-    for (int it = 0; it < n_it; ++it) {
-      const int st = it % kNQ;
-      const int rr = it / n_q;
-      const int qi = kt + (it - rr * n_q);
-      const int h = hk * p.repeats + rr;
-      const bool diag = (qi == kt);
-      if (!bar_all(wait_bounded(wc, bar_sd_full, it & 1, 8), 4, 256)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const float* lse = sLse + st * 128;
-      const float* dl = sDelta + st * 128;
-      // P^T and dS^T rows for this warpgroup's 64 query columns, packed in
-      // registers until the previous tile's products have released the tiles
-      uint32_t pk0[16], pk1[16], dk[2][16];
-      // S^T / dP^T columns of this warpgroup in four 16-column chunks; the
-      // TMEM loads of chunk c+1 are in flight while chunk c is processed.
-      auto process = [&](int c, const uint32_t (&sv)[16], const uint32_t (&dv)[16]) {
-        const int col0 = wg * 64 + c * 16;
-        const int lim = key - (qi * kBQ + col0);  // column i is masked when i < lim (key > query)
-        float lv[16], dlv[16];
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 a = *reinterpret_cast<const float4*>(lse + col0 + i);
-          const float4 d = *reinterpret_cast<const float4*>(dl + col0 + i);
-          lv[i] = a.x; lv[i + 1] = a.y; lv[i + 2] = a.z; lv[i + 3] = a.w;
-          dlv[i] = d.x; dlv[i + 1] = d.y; dlv[i + 2] = d.z; dlv[i + 3] = d.w;
-        }
-        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          // P = exp2(s * scale * log2e - lse * log2e), dS = P (dP - delta), two lanes per instruction
-          const float2 x = fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2,
-                                make_float2(lv[i], lv[i + 1]));
-          float p0 = fast_exp2(x.x);
-          float p1 = fast_exp2(x.y);
-          if (diag) {
-            if (i < lim) p0 = 0.f;
-            if (i + 1 < lim) p1 = 0.f;
-          }
-          const float2 dd = mul2(make_float2(p0, p1), sub2(make_float2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])),
-                                                           make_float2(dlv[i], dlv[i + 1])));
-          const float d0 = dd.x, d1 = dd.y;
-          if (c < 2)
-            pk0[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
-          else
-            pk1[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
-          dk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(d0, d1);
-        }
-      };
-      {
-        const uint32_t ts = tmem + lane_off + C::T_S + wg * 64;
-        const uint32_t td = tmem + lane_off + C::T_DP + wg * 64;
-        uint32_t sa[16], da[16], sb[16], db[16];
-        tmem_ld16(ts, sa);
-        tmem_ld16(td, da);
-        tmem_ld_wait_regs(sa, da);
-        tmem_ld16(ts + 16, sb);
-        tmem_ld16(td + 16, db);
-        process(0, sa, da);
-        tmem_ld_wait_regs(sb, db);
-        tmem_ld16(ts + 32, sa);
-        tmem_ld16(td + 32, da);
-        process(1, sb, db);
-        // P^T -> TMEM as soon as dV of the previous tile has released it
-        if (it > 0 && !bar_all(wait_bounded(wc, bar_pt_free, (it - 1) & 1, 7), 4, 256)) {
+    int ci = 0, n = 0;
+    for (int k = 0; ok; ++k, ++n) {
+      // one decision for both warpgroups (they meet at named barriers)
+      const int item = next_item(k, true);
+      if (!bar_all(item >= 0, 4, 256)) break;
+      const BwdItem w = bwd_item(p, item);
+      const int kt = w.kt;
+      const int key = kt * kBK + r;
+      int prev_h = 0, prev_q = 0;
+      for (int j = 0; j < w.n_it; ++j, ++ci) {
+        const int st = ci % kNQ;
+        const int rr = j / w.n_q;
+        const int qi = kt + (j - rr * w.n_q);
+        const int h = w.hk * p.repeats + rr;
+        const bool diag = (qi == kt);
+        if (!bar_all(wait_bounded(wc, bar_sd_full, ci & 1, 8), 4, 256)) {
           ok = false;
-        } else {
-          tc_fence_after();
-          tmem_st16(tmem + lane_off + C::T_PT + wg * 32, pk0);
+          break;
         }
-        tmem_ld_wait_regs(sa, da);
-        tmem_ld16(ts + 48, sb);
-        tmem_ld16(td + 48, db);
-        process(2, sa, da);
-        tmem_ld_wait_regs(sb, db);
-        process(3, sb, db);
-        if (ok) tmem_st16(tmem + lane_off + C::T_PT + wg * 32 + 16, pk1);
+        tc_fence_after();
+        const float* lse = sLse + st * 128;
+        const float* dl = sDelta + st * 128;
+        // P^T and dS^T rows for this warpgroup's 64 query columns, packed in
+        // registers until the previous tile's products have released the tiles
+        uint32_t pk0[16], pk1[16], dk[2][16];
+        // S^T / dP^T columns of this warpgroup in four 16-column chunks; the
+        // TMEM loads of chunk c+1 are in flight while chunk c is processed.
+        auto process = [&](int c, const uint32_t (&sv)[16], const uint32_t (&dv)[16]) {
+          const int col0 = wg * 64 + c * 16;
+          const int lim = key - (qi * kBQ + col0);  // column i is masked when i < lim (key > query)
+          float lv[16], dlv[16];
+  #pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(lse + col0 + i);
+            const float4 d = *reinterpret_cast<const float4*>(dl + col0 + i);
+            lv[i] = a.x; lv[i + 1] = a.y; lv[i + 2] = a.z; lv[i + 3] = a.w;
+            dlv[i] = d.x; dlv[i + 1] = d.y; dlv[i + 2] = d.z; dlv[i + 3] = d.w;
+          }
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+  #pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            // P = exp2(s * scale * log2e - lse * log2e), dS = P (dP - delta), two lanes per instruction
+            const float2 x = fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2,
+                                  make_float2(lv[i], lv[i + 1]));
+            float p0 = fast_exp2(x.x);
+            float p1 = fast_exp2(x.y);
+            if (diag) {
+              if (i < lim) p0 = 0.f;
+              if (i + 1 < lim) p1 = 0.f;
+            }
+            const float2 dd = mul2(make_float2(p0, p1), sub2(make_float2(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])),
+                                                             make_float2(dlv[i], dlv[i + 1])));
+            const float d0 = dd.x, d1 = dd.y;
+            if (c < 2)
+              pk0[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
+            else
+              pk1[(c & 1) * 8 + (i >> 1)] = pack2<T>(p0, p1);
+            dk[c >> 1][(c & 1) * 8 + (i >> 1)] = pack2<T>(d0, d1);
+          }
+        };
+        {
+          const uint32_t ts = tmem + lane_off + C::T_S + wg * 64;
+          const uint32_t td = tmem + lane_off + C::T_DP + wg * 64;
+          uint32_t sa[16], da[16], sb[16], db[16];
+          tmem_ld16(ts, sa);
+          tmem_ld16(td, da);
+          tmem_ld_wait_regs(sa, da);
+          tmem_ld16(ts + 16, sb);
+          tmem_ld16(td + 16, db);
+          process(0, sa, da);
+          tmem_ld_wait_regs(sb, db);
+          tmem_ld16(ts + 32, sa);
+          tmem_ld16(td + 32, da);
+          process(1, sb, db);
+          // P^T -> TMEM as soon as dV of the previous tile has released it
+          // (an item's first tile: the previous item's last dV is complete)
+          if (j > 0 && !bar_all(wait_bounded(wc, bar_pt_free, (ci - 1) & 1, 7), 4, 256)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            tmem_st16(tmem + lane_off + C::T_PT + wg * 32, pk0);
+          }
+          tmem_ld_wait_regs(sa, da);
+          tmem_ld16(ts + 48, sb);
+          tmem_ld16(td + 48, db);
+          process(2, sa, da);
+          tmem_ld_wait_regs(sb, db);
+          process(3, sb, db);
+          if (ok) tmem_st16(tmem + lane_off + C::T_PT + wg * 32 + 16, pk1);
+        }
+        if (!ok) break;
+        tc_fence_before();
+        mbar_arrive(bar_sd_free);
+        // dV/dK/dQ of the previous tile are complete once its dQ is: then the
+        // P/dS tiles are free and its dQ can be drained
+        if (j > 0 && !drain_dq(ci - 1, w.b, prev_h, prev_q)) {
+          ok = false;
+          break;
+        }
+  #pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col0 = wg * 64 + c * 32;
+          uint8_t* db = sDS + (col0 >> 6) * (128 * 128) + r * 128;
+          const int ch0 = (col0 & 63) >> 3;
+  #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int off = ((ch0 + q) ^ (r & 7)) * 16;
+            *reinterpret_cast<uint4*>(db + off) = make_uint4(dk[c][q * 4], dk[c][q * 4 + 1], dk[c][q * 4 + 2], dk[c][q * 4 + 3]);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        fence_proxy_async_smem();
+        mbar_arrive(bar_pds_full);
+        prev_h = h;
+        prev_q = qi;
       }
-      if (!ok) break;
-      tc_fence_before();
-      mbar_arrive(bar_sd_free);
-      // dV/dK/dQ of the previous tile are complete once its dQ is: then the
-      // P/dS tiles are free and its dQ can be drained
-      if (it > 0 && !drain_dq(it - 1, prev_h, prev_q)) {
+      if (!ok || !drain_dq(ci - 1, w.b, prev_h, prev_q)) {
         ok = false;
         break;
       }
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = wg * 64 + c * 32;
-        uint8_t* db = sDS + (col0 >> 6) * (128 * 128) + r * 128;
-        const int ch0 = (col0 & 63) >> 3;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int off = ((ch0 + q) ^ (r & 7)) * 16;
-          *reinterpret_cast<uint4*>(db + off) = make_uint4(dk[c][q * 4], dk[c][q * 4 + 1], dk[c][q * 4 + 2], dk[c][q * 4 + 3]);
+      // final: dV and dK (scaled) for this key tile, once the item's MMAs are done.
+      // They are read before this warpgroup announces the next item's first
+      // P/dS tile, so the next item's first dV/dK (which overwrite them) wait.
+      if (!bar_all(wait_bounded(wc, bar_item, n & 1, 10), 4, 256)) {
+        ok = false;
+        break;
+      }
+      {
+        tc_fence_after();
+        constexpr int kCols = D / 2;
+        uint32_t vv[kCols], kv[kCols];
+        if constexpr (kCols == 32) {
+          tmem_ld32(tmem + lane_off + C::T_DV + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(vv));
+          tmem_ld32(tmem + lane_off + C::T_DK + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(kv));
+        } else {
+          tmem_ld16(tmem + lane_off + C::T_DV + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(vv));
+          tmem_ld16(tmem + lane_off + C::T_DK + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(kv));
         }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      fence_proxy_async_smem();
-      mbar_arrive(bar_pds_full);
-      prev_h = h;
-      prev_q = qi;
-    }
-    if (ok && n_it > 0 && !drain_dq(n_it - 1, prev_h, prev_q)) ok = false;
-    // final: dV and dK (scaled) for this key tile
-    if (ok && bar_all(wait_bounded(wc, bar_done, 0, 10), 4, 256)) {
-      tc_fence_after();
-      constexpr int kCols = D / 2;
-      uint32_t vv[kCols], kv[kCols];
-      if constexpr (kCols == 32) {
-        tmem_ld32(tmem + lane_off + C::T_DV + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(vv));
-        tmem_ld32(tmem + lane_off + C::T_DK + wg * 32, *reinterpret_cast<uint32_t(*)[32]>(kv));
-      } else {
-        tmem_ld16(tmem + lane_off + C::T_DV + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(vv));
-        tmem_ld16(tmem + lane_off + C::T_DK + wg * 16, *reinterpret_cast<uint32_t(*)[16]>(kv));
-      }
-      tmem_ld_wait();
-      if (key < p.T) {
-        T* dvrow = static_cast<T*>(p.dv) + int64_t(b) * p.dvs[0] + int64_t(hk) * p.dvs[1] + int64_t(key) * p.dvs[2] +
-                   wg * kCols;
-        T* dkrow = static_cast<T*>(p.dk) + int64_t(b) * p.dks[0] + int64_t(hk) * p.dks[1] + int64_t(key) * p.dks[2] +
-                   wg * kCols;
-#pragma unroll
-        for (int q = 0; q < kCols / 8; ++q) {
-          uint4 a, c;
-          a.x = pack2<T>(__uint_as_float(vv[q * 8 + 0]), __uint_as_float(vv[q * 8 + 1]));
-          a.y = pack2<T>(__uint_as_float(vv[q * 8 + 2]), __uint_as_float(vv[q * 8 + 3]));
-          a.z = pack2<T>(__uint_as_float(vv[q * 8 + 4]), __uint_as_float(vv[q * 8 + 5]));
-          a.w = pack2<T>(__uint_as_float(vv[q * 8 + 6]), __uint_as_float(vv[q * 8 + 7]));
-          float g[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) g[i] = __uint_as_float(kv[q * 8 + i]) * p.scale;
-          if (p.rope_cos != nullptr) rope_back8<T>(g, p.rope_cos, p.rope_sin, p.rope_ld, key, (wg * kCols + q * 8) / 2);
-          c.x = pack2<T>(g[0], g[1]);
-          c.y = pack2<T>(g[2], g[3]);
-          c.z = pack2<T>(g[4], g[5]);
-          c.w = pack2<T>(g[6], g[7]);
-          *reinterpret_cast<uint4*>(dvrow + q * 8) = a;
-          *reinterpret_cast<uint4*>(dkrow + q * 8) = c;
+        tmem_ld_wait();
+        tc_fence_before();
+        if (key < p.T) {
+          T* dvrow = static_cast<T*>(p.dv) + int64_t(w.b) * p.dvs[0] + int64_t(w.hk) * p.dvs[1] +
+                     int64_t(key) * p.dvs[2] + wg * kCols;
+          T* dkrow = static_cast<T*>(p.dk) + int64_t(w.b) * p.dks[0] + int64_t(w.hk) * p.dks[1] +
+                     int64_t(key) * p.dks[2] + wg * kCols;
+  #pragma unroll
+          for (int q = 0; q < kCols / 8; ++q) {
+            uint4 a, c;
+            a.x = pack2<T>(__uint_as_float(vv[q * 8 + 0]), __uint_as_float(vv[q * 8 + 1]));
+            a.y = pack2<T>(__uint_as_float(vv[q * 8 + 2]), __uint_as_float(vv[q * 8 + 3]));
+            a.z = pack2<T>(__uint_as_float(vv[q * 8 + 4]), __uint_as_float(vv[q * 8 + 5]));
+            a.w = pack2<T>(__uint_as_float(vv[q * 8 + 6]), __uint_as_float(vv[q * 8 + 7]));
+            float g[8];
+  #pragma unroll
+            for (int i = 0; i < 8; ++i) g[i] = __uint_as_float(kv[q * 8 + i]) * p.scale;
+            if (p.rope_cos != nullptr) rope_back8<T>(g, p.rope_cos, p.rope_sin, p.rope_ld, key, (wg * kCols + q * 8) / 2);
+            c.x = pack2<T>(g[0], g[1]);
+            c.y = pack2<T>(g[2], g[3]);
+            c.z = pack2<T>(g[4], g[5]);
+            c.w = pack2<T>(g[6], g[7]);
+            *reinterpret_cast<uint4*>(dvrow + q * 8) = a;
+            *reinterpret_cast<uint4*>(dkrow + q * 8) = c;
+          }
         }
       }
     }
@@ -572,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 // preprocess: delta = rowsum(O * dO), lse2 = -lse * log2(e) (-inf past T: P = 0
 // there), stored negated so the probability is one fma + ex2; zeroes the fp32
-// dQ accumulator rows
+// dQ accumulator rows and the main kernel's work counter
 // 8 (D=64) or 4 (D=32) lanes per row, 16-byte loads.
 // ---------------------------------------------------------------------------
 template <typename T, int D>
@@ -581,9 +674,10 @@ __global__ void __launch_bounds__(256) attn_bwd_pre(const T* __restrict__ o, con
                                                     float* __restrict__ lse2, float* __restrict__ dq_acc,
                                                     int64_t os0, int64_t os1, int64_t os2,
                                                     int64_t ds0, int64_t ds1, int64_t ds2, int Hq, int seq, int Tp,
-                                                    int64_t rows) {
+                                                    int64_t rows, int* __restrict__ sched) {
   constexpr int LPR = D / 8;  // lanes per row
   const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid == 0) *sched = 0;  // the main kernel's work counter
   const int64_t row = gid / LPR;
   const int sub = (int)(gid % LPR);
   const bool valid_row = row < rows;
@@ -639,6 +733,7 @@ struct Workspace {
   float* delta;
   float* lse2;
   float* dq_acc;
+  int* sched;
   int64_t bytes;
 };
 
@@ -652,7 +747,8 @@ Workspace carve(void* base, int64_t B, int64_t Hq, int64_t T, int64_t D) {
   w.delta = reinterpret_cast<float*>(p);
   w.lse2 = reinterpret_cast<float*>(p + a);
   w.dq_acc = reinterpret_cast<float*>(p + 2 * a);
-  w.bytes = 2 * a + c;
+  w.sched = reinterpret_cast<int*>(p + 2 * a + c);
+  w.bytes = 2 * a + c + 256;
   return w;
 }
 
@@ -665,7 +761,7 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
     const int64_t threads = rows * (D / 8);
     attn_bwd_pre<T, D><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const T*>(o), static_cast<const T*>(dout), lse, ws.delta, ws.lse2, ws.dq_acc, os[0], os[1], os[2], dos[0],
-        dos[1], dos[2], prm.Hq, prm.T, prm.Tp, rows);
+        dos[1], dos[2], prm.Hq, prm.T, prm.Tp, rows, ws.sched);
     int st = check_launch("attention_bwd_pre");
     if (st != MT_OK) return st;
   }
@@ -678,8 +774,11 @@ int run_bwd(BwdParams& prm, const void* o, const void* dout, const float* lse, v
     const int64_t g = (int64_t(32) << 20) / (head_bytes > 0 ? head_bytes : 1);
     prm.n_heads = B * prm.Hkv;
     prm.group = (int)(g < 1 ? 1 : (g > prm.n_heads ? prm.n_heads : g));
-    const int64_t blocks = int64_t(prm.n_heads) * prm.n_tiles;
-    if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+    const int64_t items = int64_t(prm.n_heads) * prm.n_tiles;
+    if (items > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
+    prm.n_items = (int)items;
+    // persistent: one CTA per SM (the kernel's shared memory and TMEM allow one)
+    const int blocks = prm.n_items < get_sm_count() ? prm.n_items : get_sm_count();
     record_timing_event(0, stream);
     kern<<<(unsigned)blocks, kThreads, C::SMEM, stream>>>(prm);
     record_timing_event(1, stream);
@@ -753,6 +852,7 @@ static int attention_bwd_impl(const void* q, const void* k, const void* v, const
   prm.sw_do = swdo;
   prm.lse2 = ws.lse2;
   prm.delta = ws.delta;
+  prm.sched = ws.sched;
   prm.dk = dk;
   prm.dv = dv;
   prm.rope_cos = rope_cos;

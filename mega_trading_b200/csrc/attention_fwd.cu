@@ -10,10 +10,13 @@
 // B200 design
 //   * Work item = two consecutive 128-row query tiles ("slots") of one
 //     (batch, query head); both slots share one K/V tile stream (3 stages).
-//     Persistent: one CTA per SM (128 KB smem, all 512 TMEM columns) walks
-//     the items with a grid stride, so the next item's Q load and first
-//     S = Q K^T overlap this item's last softmax and epilogue, and barrier
-//     setup and TMEM allocation happen once per SM.
+//     Persistent: one CTA per SM (128 KB smem, all 512 TMEM columns) takes
+//     items from a global work counter (zeroed in the caller's workspace
+//     before the launch; the producer warp fetches each item and passes it
+//     to the MMA and softmax warps through a shared-memory ring), so the next
+//     item's Q load and first S = Q K^T overlap this item's last softmax and
+//     epilogue, items of unequal causal length balance across SMs, and
+//     barrier setup and TMEM allocation happen once per SM.
 //   * Warp roles: warps 0-3 / 4-7 = softmax of slot 0 / 1 (thread i owns TMEM
 //     lane = query row i of its slot), warp 8 = TMA producer (+ TMEM
 //     allocation), warp 9 = tcgen05.mma issuer.
@@ -43,6 +46,7 @@ constexpr int kBM = 128;  // query rows per slot
 constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 2;  // query tiles per CTA (consecutive tiles of one head)
 constexpr int kThreads = 352;  // 8 softmax warps, 1 TMA warp, 2 MMA warps
+constexpr int kRing = 4;       // work items announced ahead by the producer warp
 // Of every 8 pairs of scores, kPolyPairs take the polynomial exp2 on the FMA
 // pipe and the rest the MUFU ex2 (16 per clock per SM), the forward's
 // bottleneck at D=64: measured best at 2 (654 vs 646 at 1, 628 at 3 TFLOP/s
@@ -74,6 +78,7 @@ struct FwdParams {
   float* lse;
   int64_t os[4];
   int T, Hq, Hkv, repeats, n_qtiles, n_pairs, n_items;
+  int* sched;  // work counter (next item), zero at launch
   int ht_swapped;  // tensor-map coordinate order (D, H, T, B) instead of (D, T, H, B)
   float scale_log2;
   uint32_t* status;
@@ -137,8 +142,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bar_p_full = bar_s_free + kSlots;    // [kSlots]
   uint64_t* bar_o_done = bar_p_full + kSlots;    // [kSlots] (+kSlots: final MMA drains)
   uint64_t* bar_q_free = bar_o_done + 2 * kSlots;  // [kSlots]: last S of an item read its Q tile
+  uint64_t* ring_full = bar_q_free + kSlots;       // [kRing] item id published
+  uint64_t* ring_empty = ring_full + kRing;        // [kRing] item id read by the 10 consumer warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 41);
+  volatile int* ring_ids = reinterpret_cast<volatile int*>(bars + 42);  // [kRing]
 
   // Every K/V stage is released by two arrivals, one per slot: a commit after
   // the slot's P V read it, or a plain arrival from a slot that does not read
@@ -160,6 +168,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(&bar_v_full[s], 1);
       mbar_init(&bar_kv_empty[s], kSlots);
     }
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&ring_full[s], 1);
+      mbar_init(&ring_empty[s], 10);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -172,7 +184,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{p.status, abort_flag, kKernelId};
-  const int first = (int)blockIdx.x, stride = (int)gridDim.x;
+  // k-th item of this CTA (consumers): wait for the producer's announcement,
+  // release the ring entry; -1 = no more work or abort
+  auto next_item = [&](int k, bool whole_warp) -> int {
+    const int slot = k % kRing;
+    const bool got = wait_bounded(wc, &ring_full[slot], (k / kRing) & 1, 18);
+    const int it = got ? ring_ids[slot] : -1;
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || lane == 0) mbar_arrive(&ring_empty[slot]);
+    return it;
+  };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -183,7 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       int g = 0;             // K/V tiles issued by this CTA
       int nq[kSlots] = {0, 0};  // Q tiles issued per slot
       bool ok = true;
-      for (int it = first; ok && it < p.n_items; it += stride) {
+      for (int k = 0; ok; ++k) {
+        // take the next item from the work counter and announce it
+        const int slot = k % kRing;
+        if (k >= kRing && !wait_bounded(wc, &ring_empty[slot], ((k / kRing) & 1) ^ 1, 17)) break;
+        int it = atomicAdd(p.sched, 1);
+        if (it >= p.n_items) it = -1;
+        ring_ids[slot] = it;
+        mbar_arrive(&ring_full[slot]);
+        if (it < 0) break;
         const FwdItem w = fwd_item(p, it);
         for (int s = 0; s < (w.nkv1 > 0 ? 2 : 1); ++s) {
           if (nq[s] > 0 && !wait_bounded(wc, &bar_q_free[s], (nq[s] - 1) & 1, 14)) {
@@ -251,7 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       int cp = 0;  // P V products issued
       int nq = 0;  // Q tiles used
       bool ok = true;
-      for (int it = first; ok && it < p.n_items; it += stride) {
+      for (int k = 0; ok; ++k) {
+        const int it = next_item(k, false);
+        if (it < 0) break;
         const FwdItem w = fwd_item(p, it);
         const int nkv = slot ? w.nkv1 : w.nkv0;
         if (nkv > 0) {
@@ -321,7 +352,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     int cs = 0;  // S tiles read
     int cp = 0;  // P tiles written
     bool ok = true;
-    for (int it = first; ok && it < p.n_items; it += stride) {
+    for (int k = 0; ok; ++k) {
+      const int it = next_item(k, true);
+      if (it < 0) break;
       const FwdItem w = fwd_item(p, it);
       const int nkv = slot ? w.nkv1 : w.nkv0;
       if (nkv == 0) continue;
@@ -476,6 +509,11 @@ int launch_fwd(const FwdParams& prm, int B, int Hq, cudaStream_t stream) {
   auto kern = attn_fwd_kernel<T, D>;
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
+  cudaError_t err = cudaMemsetAsync(prm.sched, 0, sizeof(int), stream);  // work counter
+  if (err != cudaSuccess) {
+    set_last_error("cudaMemsetAsync", err);
+    return MT_ERR_LAUNCH;
+  }
   // persistent: one CTA per SM (the kernel's shared memory and TMEM allow one)
   const int blocks = prm.n_items < get_sm_count() ? prm.n_items : get_sm_count();
   record_timing_event(0, stream);
@@ -529,16 +567,24 @@ int check_attn_layout(const void* ptr, const int64_t* s, bool need) {
 
 using namespace mt;
 
+extern "C" int64_t mt_attention_fwd_workspace_bytes(int64_t B, int64_t Hq, int64_t T, int64_t D) {
+  (void)B, (void)Hq, (void)T, (void)D;
+  return 256;  // the persistent kernel's work counter
+}
+
 extern "C" int mt_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype,
                                 int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* qs,
                                 const int64_t* ks, const int64_t* vs, const int64_t* os, float scale,
-                                uint32_t* status, void* stream) {
+                                void* workspace, int64_t workspace_bytes, uint32_t* status, void* stream) {
   if (dtype != MT_BF16 && dtype != MT_F16) return MT_ERR_UNSUPPORTED_DTYPE;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || (Hq % Hkv) != 0) return MT_ERR_INVALID_ARGUMENT;
   if (D != 64 && D != 32) return MT_ERR_INVALID_ARGUMENT;
   if (B == 0 || T == 0) return MT_OK;
   if (lse == nullptr || status == nullptr) return MT_ERR_INVALID_ARGUMENT;
   if (B * Hq > 0x7fffffff || T > (int64_t(1) << 30)) return MT_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0 ||
+      workspace_bytes < mt_attention_fwd_workspace_bytes(B, Hq, T, D))
+    return MT_ERR_WORKSPACE;
   int st = MT_OK;
   if ((st = check_attn_layout(q, qs, true)) != MT_OK) return st;
   if ((st = check_attn_layout(k, ks, true)) != MT_OK) return st;
@@ -570,6 +616,7 @@ extern "C" int mt_attention_fwd(const void* q, const void* k, const void* v, voi
   prm.n_items = (int)(B * Hq * prm.n_pairs);
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.status = status;
+  prm.sched = static_cast<int*>(workspace);
   if (prm.n_qtiles > 65535) return MT_ERR_INVALID_ARGUMENT;
   auto s = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == MT_BF16;

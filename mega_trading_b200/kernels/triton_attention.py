@@ -27,12 +27,14 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     Hkv = k.shape[1]
     o = torch.empty_like(q)
     lse = torch.empty((B, Hq, T), device=q.device, dtype=torch.float32)
+    ws = torch.empty((int(lib.mt_attention_fwd_workspace_bytes(B, Hq, T, D)),), device=q.device, dtype=torch.uint8)
     status = _lib.status_word(q.device)
     tok = _lib.timer.start("attention_fwd", q.device, main_kernel=True)
     st = lib.mt_attention_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), _lib.dtype_code(q.dtype),
         B, Hq, Hkv, T, D, _lib.i64_array(q.stride()), _lib.i64_array(k.stride()), _lib.i64_array(v.stride()),
-        _lib.i64_array(o.stride()), float(scale), status.data_ptr(), _lib.stream_ptr(q.device),
+        _lib.i64_array(o.stride()), float(scale), ws.data_ptr(), ws.numel(), status.data_ptr(),
+        _lib.stream_ptr(q.device),
     )
     _lib.timer.stop(tok)
     _lib.check(st, "attention forward")

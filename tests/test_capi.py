@@ -44,12 +44,12 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     lib = _lib.load()
     s = _lib.i64_array([0, 0, 0, 1])
     # unsupported dtype (fp32 attention) and head_dim
-    assert lib.mt_attention_fwd(None, None, None, None, None, 0, 1, 1, 1, 8, 64, s, s, s, s, 1.0, None, None) == 2
-    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 1, 1, 1, 8, 48, s, s, s, s, 1.0, None, None) == 1
+    assert lib.mt_attention_fwd(None, None, None, None, None, 0, 1, 1, 1, 8, 64, s, s, s, s, 1.0, None, 0, None, None) == 2
+    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 1, 1, 1, 8, 48, s, s, s, s, 1.0, None, 0, None, None) == 1
     # GQA head counts that do not divide
-    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 1, 3, 2, 8, 64, s, s, s, s, 1.0, None, None) == 1
+    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 1, 3, 2, 8, 64, s, s, s, s, 1.0, None, 0, None, None) == 1
     # empty batch is a no-op
-    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 0, 2, 2, 8, 64, s, s, s, s, 1.0, None, None) == 0
+    assert lib.mt_attention_fwd(None, None, None, None, None, 2, 0, 2, 2, 8, 64, s, s, s, s, 1.0, None, 0, None, None) == 0
     # rms norm: bad dim, unsupported dtype combination
     assert lib.mt_rms_norm_fwd(None, 2, None, 2, None, 2, None, 4, 0, 1e-5, None) == 1
     assert lib.mt_rms_norm_fwd(ctypes.c_void_p(16), 2, None, 1, ctypes.c_void_p(16), 0, None, 4, 8, 1e-5, None) == 2
@@ -62,6 +62,7 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
                                12, None, None, None, 0, None, None) == 3
     assert lib.mt_fused_ce_workspace_bytes(1024, 21504) > 1024 * 4
     assert lib.mt_attention_bwd_workspace_bytes(2, 4, 130, 64) >= 2 * 4 * 256 * 64 * 4
+    assert lib.mt_attention_fwd_workspace_bytes(2, 4, 130, 64) >= 4
 
 
 @pytest.mark.parametrize("name", ["mt_rms_norm_fwd", "mt_attention_fwd", "mt_fused_ce_fwd"])
