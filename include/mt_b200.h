@@ -322,6 +322,43 @@ MT_API int mt_fused_ce_grad_logits(const void* hidden, const void* weight,
                                    int64_t K, const float* lse2_scal, const float* grad_out,
                                    void* dz, int64_t dz_ld, uint32_t* status, void* stream);
 
+/* ---------------------------------------------------------------------
+ * Fused AdamW with 16-bit weight copies   replaces torch.optim.AdamW(fused=True)
+ *   (src/mega_trading/trainer.py:535-545) plus the per-forward bf16 weight
+ *   casts of the reference's autocast (trainer.py:336); no counterpart kernel
+ *   in the reference.
+ * One launch updates every tensor of the table (decoupled weight decay,
+ * bias-corrected moments, torch.optim.AdamW semantics):
+ *   p -= lr*wd*p ; m = b1*m + (1-b1)*g ; v = b2*v + (1-b2)*g*g ;
+ *   p -= step_size * m / (sqrt(v) / bias_correction2_sqrt + eps)
+ * with step_size = lr / (1 - b1^t), bias_correction2_sqrt = sqrt(1 - b2^t)
+ * computed by the caller for the tensors' common step t.  Then, when shadow is
+ * not NULL, the updated value rounded to shadow_dtype (bf16 or fp16) is
+ * stored at shadow[(j / shadow_block) * shadow_stride + j % shadow_block] for
+ * element j: shadow_block = numel for a contiguous copy; a copy interleaved
+ * with other tensors in blocks of rows uses the block size and the distance
+ * between its blocks (shadow_block < 2^32).
+ * tensors: DEVICE array of n_tensors entries sorted by offset, offsets the
+ * prefix sums of numel (offset[0] = 0); total = sum of numel.  All fp32
+ * pointers distinct per tensor.
+ * ------------------------------------------------------------------- */
+typedef struct MtAdamWTensor {
+  float* param;          /* fp32 master weights, updated in place */
+  const float* grad;     /* fp32 gradient                          */
+  float* exp_avg;        /* fp32 first moment                      */
+  float* exp_avg_sq;     /* fp32 second moment                     */
+  void* shadow;          /* 16-bit copy of the updated weights, or NULL */
+  int64_t numel;
+  int64_t shadow_block;
+  int64_t shadow_stride;
+  int64_t offset;        /* first index of this tensor in the flattened space */
+} MtAdamWTensor;
+
+MT_API int mt_adamw_step(const MtAdamWTensor* tensors, int n_tensors, int64_t total,
+                         int shadow_dtype, float lr, float beta1, float beta2, float eps,
+                         float weight_decay, float step_size, float bias_correction2_sqrt,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

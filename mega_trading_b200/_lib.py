@@ -68,6 +68,8 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "mt_swiglu_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp]),
     "mt_swiglu_packed_fwd": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
     "mt_swiglu_packed_bwd": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "mt_adamw_step": (c_int, [c_vp, c_int, c_i64, c_int, c_float, c_float, c_float, c_float, c_float, c_float,
+                              c_float, c_vp]),
     "mt_attention_fwd_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
     "mt_attention_fwd": (
         c_int,

@@ -10,7 +10,11 @@ bf16 GEMMs with fp32 accumulation, as in the reference.
 
 Precision follows the reference's Accelerate bf16 autocast (``trainer.py:336``,
 ``:1009-1023``): fp32 master weights, bf16 GEMM operands, fp32 residual stream.
-Dropout is 0 (the reference's rtx configuration, ``configs/rtx.yaml``).
+The bf16 operands are :class:`~mega_trading_b200.optim.PackedWeights` copies in
+the layouts the GEMMs read (q/k/v stacked, gate/up interleaved); the fused
+optimizer (``optim.AdamWShadow``) rewrites them as it updates the weights, so
+the forward does no casting.  Dropout is 0 (the reference's rtx
+configuration, ``configs/rtx.yaml``).
 """
 
 from __future__ import annotations
@@ -23,9 +27,10 @@ from torch import nn
 
 from .kernels import triton_attention as _attn
 from .kernels import triton_ops as _ops
-from .kernels.fused_blocks import (interleave_gate_up, qkv_proj_rope_attention, qkv_rope_attention,
+from .kernels.fused_blocks import (GATE_BLOCK, qkv_proj_rope_attention, qkv_rope_attention,
                                    qkv_rope_gemm_supported, swiglu_mlp, swiglu_mlp_supported, swiglu_packed)
 from .kernels.fused_ce import fused_linear_cross_entropy
+from .optim import PackedWeights
 
 
 @dataclass(frozen=True)
@@ -75,6 +80,16 @@ def _w(p: torch.Tensor) -> torch.Tensor:
     return p if p.dtype == _BF16 else p.to(_BF16)
 
 
+def _packed(module: nn.Module, key: str, params: list[nn.Parameter], kind: str = "single") -> PackedWeights:
+    """The module's cached bf16 copy of ``params`` (rebuilt if the parameters were replaced)."""
+    pw = module.__dict__.get(key)
+    if pw is None or len(pw.params) != len(params) or any(a is not b for a, b in zip(pw.params, params)) \
+            or pw.kind != kind:
+        pw = PackedWeights(params, kind, block_rows=GATE_BLOCK)
+        module.__dict__[key] = pw
+    return pw
+
+
 class RMSNorm(nn.Module):
     def __init__(self, dim: int, eps: float) -> None:
         super().__init__()
@@ -101,11 +116,16 @@ class LlamaAttention(nn.Module):
         self.register_buffer("cos", freqs.cos().to(_BF16), persistent=False)
         self.register_buffer("sin", freqs.sin().to(_BF16), persistent=False)
 
+    def packed_weights(self) -> list[PackedWeights]:
+        return [_packed(self, "_qkv_bf16", [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], "rows"),
+                _packed(self, "_o_bf16", [self.o_proj.weight])]
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, H = x.shape
         # one projection GEMM against [q_proj; k_proj; v_proj]; RoPE + attention
         # read the packed output in place and write one packed gradient
-        w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], dim=0).to(_BF16)
+        pw_qkv, pw_o = self.packed_weights()
+        w_qkv = pw_qkv.get()
         if qkv_rope_gemm_supported(self.heads, self.kv_heads, self.head_dim, H):
             # RoPE in the projection GEMM's epilogue (tcgen05)
             o = qkv_proj_rope_attention(x, w_qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
@@ -113,7 +133,7 @@ class LlamaAttention(nn.Module):
             qkv = F.linear(x, w_qkv)
             o = qkv_rope_attention(qkv, self.cos, self.sin, self.heads, self.kv_heads, self.head_dim)
         # o is stored [B, T, H, D]: the transpose is free
-        return F.linear(o.transpose(1, 2).reshape(B, T, H), _w(self.o_proj.weight))
+        return F.linear(o.transpose(1, 2).reshape(B, T, H), pw_o.get())
 
     def forward_unfused(self, x: torch.Tensor) -> torch.Tensor:
         """Operator-by-operator path through the reference API mirror (same math)."""
@@ -133,15 +153,21 @@ class SwiGLU(nn.Module):
         self.w2 = nn.Linear(cfg.intermediate_dim, cfg.hidden_dim, bias=False)
         self.w3 = nn.Linear(cfg.hidden_dim, cfg.intermediate_dim, bias=False)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def packed_weights(self) -> list[PackedWeights]:
         inter, hidden = self.w1.weight.shape
-        if swiglu_mlp_supported(inter, hidden):
+        # gate/up interleaved in GATE_BLOCK-row blocks for the fused GEMM, else stacked
+        kind = "interleave" if swiglu_mlp_supported(inter, hidden) else "rows"
+        return [_packed(self, "_w13_bf16", [self.w1.weight, self.w3.weight], kind),
+                _packed(self, "_w2_bf16", [self.w2.weight])]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        pw13, pw2 = self.packed_weights()
+        if pw13.kind == "interleave":
             # gate inside the projection GEMMs (tcgen05): w1 || w3 interleaved
-            w13 = interleave_gate_up(self.w1.weight, self.w3.weight).to(_BF16)
-            return swiglu_mlp(x, w13, _w(self.w2.weight))
+            return swiglu_mlp(x, pw13.get(), pw2.get())
         # one GEMM against [w1; w3]; the gate reads [gate | up] in place
-        gu = F.linear(x, torch.cat([self.w1.weight, self.w3.weight], dim=0).to(_BF16))
-        return F.linear(swiglu_packed(gu), _w(self.w2.weight))
+        gu = F.linear(x, pw13.get())
+        return F.linear(swiglu_packed(gu), pw2.get())
 
     def forward_unfused(self, x: torch.Tensor) -> torch.Tensor:
         gate = F.linear(x, _w(self.w1.weight))
@@ -199,11 +225,18 @@ class TradingModelB200(nn.Module):
             h, x = block.forward_fused(h, x, nxt)
         return x
 
+    def packed_weights(self) -> list[PackedWeights]:
+        """Every bf16 GEMM operand copy of the model (handed to ``optim.AdamWShadow``)."""
+        out = [_packed(self, "_out_bf16", [self.output.weight])]
+        for block in self.blocks:
+            out += block.attention.packed_weights() + block.feed_forward.packed_weights()
+        return out
+
     def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
         """Mean next-token loss when ``labels`` is given (the training entry), else logits."""
         if labels is not None:
             return self.forward_with_loss(input_ids, labels, return_logits=False)[0]
-        return F.linear(self.hidden_states(input_ids), _w(self.output.weight)).float()
+        return F.linear(self.hidden_states(input_ids), self.packed_weights()[0].get()).float()
 
     def forward_with_loss(self, input_ids: torch.Tensor, labels: torch.Tensor, *, return_logits: bool = False,
                           ignore_index: int = -100):
@@ -212,11 +245,11 @@ class TradingModelB200(nn.Module):
         if labels.shape != input_ids.shape:
             raise ValueError("labels must match input_ids shape")
         normed = self.hidden_states(input_ids)
+        w_out = _packed(self, "_out_bf16", [self.output.weight]).get()
         if not return_logits:
             flat = normed.reshape(-1, normed.shape[-1])
-            return fused_linear_cross_entropy(flat, _w(self.output.weight), labels.reshape(-1),
-                                              ignore_index=ignore_index), None
-        logits = F.linear(normed, _w(self.output.weight)).float()
+            return fused_linear_cross_entropy(flat, w_out, labels.reshape(-1), ignore_index=ignore_index), None
+        logits = F.linear(normed, w_out).float()
         loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), labels.reshape(-1), ignore_index=ignore_index)
         return loss, logits
 

@@ -4,7 +4,8 @@ Mirrors the reference's hot loop (``src/mega_trading/trainer.py:324-345``):
 forward, next-token cross-entropy (here the fused kernel, closing the wiring
 gap at ``trainer.py:337-338``), backward with the bucketed NCCL gradient
 all-reduce overlapped with backward (torch DDP, as Accelerate's default
-``trainer.py:1009-1023, :300-308``), fused AdamW (``trainer.py:537-545``).
+``trainer.py:1009-1023, :300-308``), fused AdamW (``trainer.py:537-545``; on
+the GPU ``optim.AdamWShadow``, which also writes the bf16 weight copies).
 One process per GPU; the batch is split across ranks and, inside a rank,
 across micro-batches (gradient accumulation, all-reduce on the last one).
 The all-reduce is the only collective of the step.
@@ -20,6 +21,7 @@ import torch
 import torch.distributed as dist
 
 from .model import ModelConfig, TradingModelB200
+from .optim import AdamWShadow
 
 
 def init_distributed(backend: str = "nccl", timeout_s: int = 300) -> tuple[int, int, int]:
@@ -63,10 +65,15 @@ class Trainer:
             )
         else:
             self.engine = self.model
-        self.opt = torch.optim.AdamW(
-            self.model.parameters(), lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=weight_decay,
-            fused=device.type == "cuda",
-        )
+        if device.type == "cuda" and hasattr(self.model, "packed_weights"):
+            # one kernel per step: the AdamW update plus the bf16 GEMM-operand copies
+            self.opt = AdamWShadow(self.model.parameters(), lr=lr, betas=(0.9, 0.999), eps=1e-8,
+                                   weight_decay=weight_decay, packed=self.model.packed_weights())
+        else:
+            self.opt = torch.optim.AdamW(
+                self.model.parameters(), lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=weight_decay,
+                fused=device.type == "cuda",
+            )
 
     def step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         """One optimizer step over this rank's ``[B, T]`` batch; returns the mean loss (device scalar,

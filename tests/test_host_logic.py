@@ -130,3 +130,80 @@ def test_fused_projection_paths_follow_the_shapes():
     assert qkv_rope_gemm_supported(16, 4, 64, 1024)     # config 4: 1536 columns
     assert not qkv_rope_gemm_supported(8, 2, 32, 256)   # config 0: 384 columns -> cuBLAS + RoPE kernel
     assert not qkv_rope_gemm_supported(4, 2, 48, 256)   # head_dim 48
+
+
+def test_packed_weight_copies_follow_the_gemm_layouts():
+    """The element map the fused optimizer writes through (block / stride / start per
+    parameter) reproduces the packed layouts, and the packed copy's gradient reaches
+    each fp32 parameter unchanged."""
+    from mega_trading_b200.kernels.fused_blocks import GATE_BLOCK, interleave_gate_up
+    from mega_trading_b200.optim import PackedWeights
+
+    torch.manual_seed(0)
+    w1 = torch.nn.Parameter(torch.randn(2 * GATE_BLOCK, 48))
+    w3 = torch.nn.Parameter(torch.randn(2 * GATE_BLOCK, 48))
+    q = torch.nn.Parameter(torch.randn(96, 48))
+    k = torch.nn.Parameter(torch.randn(32, 48))
+    v = torch.nn.Parameter(torch.randn(32, 48))
+    cases = [(PackedWeights([w1, w3], "interleave", GATE_BLOCK), interleave_gate_up(w1, w3)),
+             (PackedWeights([q, k, v], "rows"), torch.cat([q, k, v])),
+             (PackedWeights([q]), q)]
+    for pw, ref in cases:
+        packed = pw.pack()
+        assert packed.dtype == torch.bfloat16 and torch.equal(packed, ref.detach().to(torch.bfloat16))
+        flat = packed.reshape(-1)
+        for part in pw.parts():
+            src = part.param.detach().reshape(-1).to(torch.bfloat16)
+            j = torch.arange(src.numel())
+            assert torch.equal(flat[part.start + (j // part.block) * part.stride + j % part.block], src)
+        g = torch.randn(packed.shape).to(torch.bfloat16)
+        for p in pw.params:
+            p.grad = None
+        pw.get().backward(g)
+        ref_params = [p.detach().clone().requires_grad_() for p in pw.params]
+        if pw.kind == "interleave":
+            interleave_gate_up(*ref_params).to(torch.bfloat16).backward(g)
+        elif len(ref_params) > 1:
+            torch.cat(ref_params).to(torch.bfloat16).backward(g)
+        else:
+            ref_params[0].to(torch.bfloat16).backward(g)
+        for p, r in zip(pw.params, ref_params):
+            assert p.grad.dtype == torch.float32 and torch.equal(p.grad, r.grad)
+
+
+def test_packed_weight_copy_is_rebuilt_unless_the_fused_optimizer_owns_it():
+    import gc
+
+    from mega_trading_b200.optim import AdamWShadow, PackedWeights
+
+    w = torch.nn.Parameter(torch.zeros(4, 8))
+    pw = PackedWeights([w])
+    assert torch.equal(pw.get(), torch.zeros(4, 8, dtype=torch.bfloat16))
+    # torch's fused AdamW moves weights without advancing version counters: an
+    # unowned copy is rebuilt in every forward
+    w.grad = torch.ones(4, 8)
+    torch.optim.AdamW([w], lr=0.5, fused=True).step()
+    assert w._version == 0 and torch.equal(pw.get(), w.detach().to(torch.bfloat16))
+    # owned: reused until a version counter moves
+    opt = AdamWShadow([w], lr=1e-3, packed=[pw])
+    assert pw.owned and not pw._stale()
+    with torch.no_grad():
+        w.fill_(1.5)  # e.g. load_state_dict
+    assert pw._stale() and torch.equal(pw.get(), torch.full((4, 8), 1.5, dtype=torch.bfloat16))
+    del opt
+    gc.collect()
+    assert not pw.owned and pw._stale()
+    with pytest.raises(ValueError, match="stepped by this optimizer"):
+        AdamWShadow([torch.nn.Parameter(torch.zeros(2))], packed=[pw])
+
+
+def test_fused_adamw_refuses_cpu_parameters():
+    from mega_trading_b200.optim import AdamWShadow
+
+    w = torch.nn.Parameter(torch.zeros(4))
+    w.grad = torch.ones(4)
+    opt = AdamWShadow([w], lr=1e-3)
+    with pytest.raises(RuntimeError, match="fp32 CUDA"):
+        opt.step()
+    with pytest.raises(ValueError):
+        AdamWShadow([w], lr=-1.0)
