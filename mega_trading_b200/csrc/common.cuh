@@ -243,6 +243,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait on a local mbarrier whose arrivals may come from the other CTA of the pair.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA,
 // tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -273,6 +284,22 @@ __device__ __forceinline__ bool wait_bounded(const WaitCtx& ctx, uint64_t* bar, 
   while (true) {
     if (*ctx.abort_flag) return false;
     if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(ctx.status, 0u, (ctx.kernel_id << 16) | site);
+      *ctx.abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// wait_bounded for a barrier that receives arrivals from the other CTA of a pair.
+__device__ __forceinline__ bool wait_bounded_cluster(const WaitCtx& ctx, uint64_t* bar, uint32_t parity,
+                                                     uint32_t site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    if (*ctx.abort_flag) return false;
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if (clock64() - t0 > kWaitCycles) {
       atomicCAS(ctx.status, 0u, (ctx.kernel_id << 16) | site);
       *ctx.abort_flag = 1;
@@ -390,6 +417,81 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
 // thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// CTA pairs (cluster of 2, tcgen05 cta_group::2): the pair shares one MMA of
+// M = 256 whose A rows and B columns are split between the two CTAs' shared
+// memory and whose accumulator rows live in the two CTAs' TMEM.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs (like __syncthreads across the pair).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of this CTA's variable `p` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of another CTA of the cluster (address from cluster_addr).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Address of this CTA's barrier `bar` in the even CTA of its pair (the pair's
+// leader): the shared::cluster window puts the odd CTA one bit-24 step above.
+__device__ __forceinline__ uint32_t leader_addr(const void* bar) { return smem_u32(bar) & 0xFEFFFFFFu; }
+// TMA tile load into this CTA's shared memory whose completion (bytes) is
+// counted on the pair leader's mbarrier (address from leader_addr).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader_bar, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(leader_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+// Paired TMEM allocation: the same warp of both CTAs, the same destination offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Paired MMA (issued by the even CTA only): D rows 0-127 in CTA 0's TMEM,
+// 128-255 in CTA 1's; each CTA's shared memory holds its A rows and its half
+// of B's N columns at the descriptors' (CTA-local) addresses.
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at this offset in every CTA of `cta_mask` when the
+// paired MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+// Same, on this CTA's barrier only.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 

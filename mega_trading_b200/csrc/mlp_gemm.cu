@@ -34,6 +34,20 @@
 // Warp roles (352 threads): warps 0-7 epilogue in two warpgroups taking
 // alternate 32-column steps (each with its own staging boxes), 8 TMA producer
 // (+ TMEM allocation), 9 MMA issuer, 10 epilogue-input loader (MODE 1).
+//
+// CTA pairs (PAIR: MODE 0 with M > 128): a cluster of two CTAs computes a
+// 256 x 256 tile with tcgen05 cta_group::2 MMAs (M = 256).  Each CTA stages
+// its own 128 A rows and one 128-row half of B (32 KB per stage instead of
+// 48 KB: a single CTA streaming a whole 128 x 256 tile needs ~1.5x the
+// shared-memory bandwidth the tensor core leaves for it), and holds its 128
+// accumulator rows in its own TMEM.  Both CTAs' stage loads (cta_group::2
+// TMA, no multicast) complete on the even CTA's full barrier, which expects
+// both CTAs' bytes; the even CTA issues the MMAs and commits to both CTAs'
+// empty / accumulator barriers (multicast commit); both epilogues release the
+// accumulator to the even CTA.  Before teardown the odd CTA waits (bounded)
+// for the release of every stage it loaded, which the even CTA's MMAs can
+// only signal after those bytes landed.  (MODE 1 is bound by its gate/up HBM
+// traffic and MODE 2 measured faster unpaired, so they stay single-CTA.)
 #include <algorithm>
 #include <cmath>
 #include <initializer_list>
@@ -52,11 +66,13 @@ constexpr int kGB = 128;   // gate / up interleave block
 constexpr int kThreads = 352;
 constexpr uint32_t kKernelId = 6;
 
-template <int MODE>
+template <int MODE, bool PAIR>
 struct GCfg {
-  static constexpr int NST = MODE == 2 ? 4 : 3;
-  static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
-  static constexpr int B_BYTES = kBN * kBK * 2;  // 32 KB
+  static constexpr int NST = PAIR ? (MODE == 0 ? 5 : (MODE == 1 ? 4 : 6)) : (MODE == 2 ? 4 : 3);
+  static constexpr int TM = PAIR ? 2 * kBM : kBM;      // tile rows (the pair's M)
+  static constexpr int B_ROWS = PAIR ? kBN / 2 : kBN;  // rows of B this CTA stages
+  static constexpr int A_BYTES = kBM * kBK * 2;        // 16 KB
+  static constexpr int B_BYTES = B_ROWS * kBK * 2;     // 16 KB (pair) or 32 KB
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BOX = kBM * kEC * 2;      // [128 rows][32 cols] 16-bit = 8 KB, 64 B rows
   static constexpr int N_OUT = MODE == 0 ? 3 : (MODE == 1 ? 2 : 1);
@@ -84,9 +100,9 @@ struct GemmParams {
 // 64B-swizzled [rows][32] 16-bit box: byte offset of 16-byte chunk j of row r.
 __device__ __forceinline__ int box_off(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
 
-template <typename T, int MODE>
+template <typename T, int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using C = GCfg<MODE>;
+  using C = GCfg<MODE, PAIR>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = warp_id();
   const int lane = lane_id();
@@ -105,14 +121,22 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 29);
 
+  // pair geometry: the even CTA (rank 0) leads; a "unit" is a pair or a lone CTA
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int row_off = (int)rank * kBM;  // this CTA's first row inside a tile
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NST; ++s) {
+      // a pair's stage is full once the leader armed it and both CTAs' bytes landed
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&acc_full[s], 1);
-      mbar_init(&acc_empty[s], 256);
+      mbar_init(&acc_empty[s], PAIR ? 16 : 8);  // one arrival per epilogue warp (of both CTAs)
     }
     mbar_init(fin, 1);
     for (int s = 0; s < C::E; ++s) {
@@ -123,14 +147,29 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
     fence_barrier_init();
   }
   if (warp == 8) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{p.status, abort_flag, kKernelId};
+  // waits on barriers the partner CTA (or its tensor core) signals
+  auto wait_x = [&](uint64_t* bar, uint32_t parity, uint32_t site) {
+    if constexpr (PAIR)
+      return wait_bounded_cluster(wc, bar, parity, site);
+    else
+      return wait_bounded(wc, bar, parity, site);
+  };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -139,40 +178,55 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
       tma_prefetch_desc(&p.tm_b);
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+      for (int t = unit; ok && t < p.n_tiles; t += n_units) {
         const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
         for (int kc = 0; kc < p.n_k; ++kc, ++it) {
           const int st = it % C::NST;
-          if (it >= C::NST && !wait_bounded(wc, &empty[st], ((it / C::NST) & 1) ^ 1, 1)) {
+          if (it >= C::NST && !wait_x(&empty[st], ((it / C::NST) & 1) ^ 1, 1)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + st * C::STAGE;
-          mbar_arrive_expect_tx(&full[st], C::STAGE);
-          tma_load_2d(sa, &p.tm_a, &full[st], kc * kBK, mt * kBM);
-          tma_load_2d(sa + C::A_BYTES, &p.tm_b, &full[st], kc * kBK, nt * kBN);
+          if constexpr (PAIR) {
+            if (leader) mbar_arrive_expect_tx(&full[st], 2 * C::STAGE);
+            const uint32_t bar = leader_addr(&full[st]);
+            tma_load_2d_pair(sa, &p.tm_a, bar, kc * kBK, mt * C::TM + row_off);
+            tma_load_2d_pair(sa + C::A_BYTES, &p.tm_b, bar, kc * kBK, nt * kBN + (int)rank * C::B_ROWS);
+          } else {
+            mbar_arrive_expect_tx(&full[st], C::STAGE);
+            tma_load_2d(sa, &p.tm_a, &full[st], kc * kBK, mt * C::TM + row_off);
+            tma_load_2d(sa + C::A_BYTES, &p.tm_b, &full[st], kc * kBK, nt * kBN + (int)rank * C::B_ROWS);
+          }
         }
+      }
+      if (PAIR && !leader) {
+        // the odd CTA's loads complete on the leader's barrier: wait until the
+        // leader's MMAs released every stage loaded here (bounded)
+        for (int j = (it > C::NST ? it - C::NST : 0); j < it; ++j)
+          wait_drain(wc, &empty[j % C::NST], (j / C::NST) & 1, 15);
       }
       if (*abort_flag) {
         for (int j = (it > C::NST ? it - C::NST : 0); j < it; ++j) wait_drain(wc, &full[j % C::NST], (j / C::NST) & 1, 11);
       }
     }
+  } else if (warp == 9 && PAIR && !leader) {
+    // the odd CTA issues no MMAs
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr int kBf16 = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      constexpr uint32_t idesc = make_idesc(kBM, kBN, kBf16, 0, 0);
+      constexpr uint32_t idesc = make_idesc(C::TM, kBN, kBf16, 0, 0);
       const uint32_t base = smem_u32(smem);
       int it = 0, lt = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x, ++lt) {
+      for (int t = unit; ok && t < p.n_tiles; t += n_units, ++lt) {
         const int buf = lt & 1;
-        if (lt >= 2 && !wait_bounded(wc, &acc_empty[buf], ((lt >> 1) & 1) ^ 1, 2)) break;
+        if (lt >= 2 && !wait_x(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * kBN;
         for (int kc = 0; kc < p.n_k; ++kc, ++it) {
           const int st = it % C::NST;
-          if (!wait_bounded(wc, &full[st], (it / C::NST) & 1, 3)) {
+          if (!wait_x(&full[st], (it / C::NST) & 1, 3)) {
             ok = false;
             break;
           }
@@ -180,14 +234,30 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           const uint32_t a = base + st * C::STAGE;
           const uint32_t b = a + C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_ss(d, make_sdesc(a + kk * 32, 16, 1024, kSwizzle128), make_sdesc(b + kk * 32, 16, 1024, kSwizzle128),
-                    idesc, (kc > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[st]);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = make_sdesc(a + kk * 32, 16, 1024, kSwizzle128);
+            const uint64_t bd = make_sdesc(b + kk * 32, 16, 1024, kSwizzle128);
+            if constexpr (PAIR)
+              umma_ss_pair(d, ad, bd, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+            else
+              umma_ss(d, ad, bd, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+          }
+          if constexpr (PAIR)
+            umma_commit_pair_mc(&empty[st], 3);
+          else
+            umma_commit(&empty[st]);
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok) {
+          if constexpr (PAIR)
+            umma_commit_pair_mc(&acc_full[buf], 3);
+          else
+            umma_commit(&acc_full[buf]);
+        }
       }
-      umma_commit(fin);
+      if constexpr (PAIR)
+        umma_commit_pair(fin);
+      else
+        umma_commit(fin);
       wait_drain(wc, fin, 0, 13);
     }
   } else if (warp == 10) {
@@ -197,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
         tma_prefetch_desc(&p.tm_gu);
         int q = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+        for (int t = unit; ok && t < p.n_tiles; t += n_units) {
           const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
           for (int c = 0; c < kBN / kEC; ++c, ++q) {
             const int slot = q % C::E;
@@ -209,8 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
             const int gcol = (col / kGB) * (2 * kGB) + (col % kGB);
             uint8_t* dst = smem + C::OFF_IN + slot * 2 * C::BOX;
             mbar_arrive_expect_tx(&in_full[slot], 2 * C::BOX);
-            tma_load_2d(dst, &p.tm_gu, &in_full[slot], gcol, mt * kBM);
-            tma_load_2d(dst + C::BOX, &p.tm_gu, &in_full[slot], gcol + kGB, mt * kBM);
+            tma_load_2d(dst, &p.tm_gu, &in_full[slot], gcol, mt * C::TM + row_off);
+            tma_load_2d(dst + C::BOX, &p.tm_gu, &in_full[slot], gcol + kGB, mt * C::TM + row_off);
           }
         }
         if (*abort_flag) {
@@ -226,11 +296,26 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
     uint8_t* out = smem + C::OFF_OUT + wg * C::N_OUT * C::BOX;
     bool ok = true;
     int lt = 0;
-    for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x, ++lt) {
+    // the accumulator buffer is released by one arrival per warp (at the
+    // leader's barrier for a pair)
+    const uint32_t acc_empty_x[2] = {PAIR ? cluster_addr(&acc_empty[0], 0) : 0u,
+                                     PAIR ? cluster_addr(&acc_empty[1], 0) : 0u};
+    auto release_acc = [&](int b) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_remote(acc_empty_x[b]);
+        else
+          mbar_arrive(&acc_empty[b]);
+      }
+    };
+    for (int t = unit; ok && t < p.n_tiles; t += n_units, ++lt) {
       const int qt = lt * (kBN / kEC);  // MODE 1: first input-ring step of this tile
       const int mt = t / p.n_nt, nt = t - mt * p.n_nt;
+      const int row0 = mt * C::TM + row_off;  // first row of this CTA's part of the tile
       const int buf = lt & 1;
-      if (!__all_sync(0xffffffffu, wait_bounded(wc, &acc_full[buf], (lt >> 1) & 1, 8))) {
+      if (!__all_sync(0xffffffffu, wait_x(&acc_full[buf], (lt >> 1) & 1, 8))) {
         ok = false;
         break;
       }
@@ -243,10 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           tmem_ld32(acc + c * kEC, zg);
           tmem_ld32(acc + kGB + c * kEC, zu);
           tmem_ld_wait();
-          if (c + 2 >= kGB / kEC) {
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-          }
+          if (c + 2 >= kGB / kEC) release_acc(buf);
           uint32_t pg[16], pu[16], py[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
@@ -272,24 +354,21 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           named_bar_sync(1 + wg, 128);
           if (r == 0) {
             const int gcol = nt * kBN + c * kEC;  // interleaved gate/up columns of this tile
-            tma_store_2d(&p.tm_gu, out, gcol, mt * kBM);
-            tma_store_2d(&p.tm_gu, out + C::BOX, gcol + kGB, mt * kBM);
-            tma_store_2d(&p.tm_out, out + 2 * C::BOX, nt * kGB + c * kEC, mt * kBM);
+            tma_store_2d(&p.tm_gu, out, gcol, row0);
+            tma_store_2d(&p.tm_gu, out + C::BOX, gcol + kGB, row0);
+            tma_store_2d(&p.tm_out, out + 2 * C::BOX, nt * kGB + c * kEC, row0);
             bulk_commit_group();
           }
         }
       } else if constexpr (MODE == 2) {
-        const int row = mt * kBM + r;
+        const int row = row0 + r;
         const int t_pos = row % p.seq;
 #pragma unroll 1
         for (int c = wg; c < kBN / kEC; c += 2) {
           uint32_t z[32];
           tmem_ld32(acc + c * kEC, z);
           tmem_ld_wait();
-          if (c + 2 >= kBN / kEC) {
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-          }
+          if (c + 2 >= kBN / kEC) release_acc(buf);
           const int col0 = nt * kBN + c * kEC;
           uint32_t pk[16];
           if (col0 < p.rot_cols) {
@@ -328,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           fence_proxy_async_smem();
           named_bar_sync(1 + wg, 128);
           if (r == 0) {
-            tma_store_2d(&p.tm_out, out, col0, mt * kBM);
+            tma_store_2d(&p.tm_out, out, col0, row0);
             bulk_commit_group();
           }
         }
@@ -339,10 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           uint32_t zd[32];
           tmem_ld32(acc + c * kEC, zd);
           tmem_ld_wait();
-          if (c + 2 >= kBN / kEC) {
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-          }
+          if (c + 2 >= kBN / kEC) release_acc(buf);
           const int slot = q % C::E;
           if (!__all_sync(0xffffffffu, wait_bounded(wc, &in_full[slot], (q / C::E) & 1, 9))) {
             ok = false;
@@ -387,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
           if (r == 0) {
             const int col = nt * kBN + c * kEC;
             const int gcol = (col / kGB) * (2 * kGB) + (col % kGB);
-            tma_store_2d(&p.tm_out, out, gcol, mt * kBM);
-            tma_store_2d(&p.tm_out, out + C::BOX, gcol + kGB, mt * kBM);
+            tma_store_2d(&p.tm_out, out, gcol, row0);
+            tma_store_2d(&p.tm_out, out + C::BOX, gcol + kGB, row0);
             bulk_commit_group();
           }
         }
@@ -399,10 +475,16 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // the leader's MMAs into this CTA are done; no arrival is still in flight
+  else
+    __syncthreads();
   if (warp == 8) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
@@ -425,23 +507,62 @@ int validate(int dtype, int64_t M, int64_t K, int64_t I, std::initializer_list<c
   return MT_OK;
 }
 
-template <int MODE>
-int launch(GemmParams& prm, int dtype, int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
-  const int64_t n_mt = (M + kBM - 1) / kBM;
+// CTA pairs for the gate/up projection whenever the rows fill more than one
+// 128-row tile.
+bool use_pair(int MODE, int64_t M) { return MODE == 0 && M > kBM; }
+
+template <int MODE, bool PAIR>
+int launch_impl(GemmParams& prm, int dtype, int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
+  using C = GCfg<MODE, PAIR>;
+  const int64_t n_mt = (M + C::TM - 1) / C::TM;
   prm.M = (int)M;
   prm.n_nt = (int)(N / kBN);
   prm.n_tiles = (int)(n_mt * prm.n_nt);
   prm.n_k = (int)((K + kBK - 1) / kBK);
   if (n_mt * prm.n_nt > 0x7fffffffLL) return MT_ERR_INVALID_ARGUMENT;
-  const int grid = (int)std::min<int64_t>(prm.n_tiles, get_sm_count());
-  using C = GCfg<MODE>;
+  const int per_unit = PAIR ? 2 : 1;
+  const int units = (int)std::min<int64_t>(prm.n_tiles, get_sm_count() / per_unit);
   const bool bf = dtype == MT_BF16;
-  auto kern = bf ? mlp_gemm_kernel<__nv_bfloat16, MODE> : mlp_gemm_kernel<__half, MODE>;
+  auto kern = bf ? mlp_gemm_kernel<__nv_bfloat16, MODE, PAIR> : mlp_gemm_kernel<__half, MODE, PAIR>;
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
-  kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
-  return check_launch(MODE == 0 ? "mlp_gemm_swiglu_fwd" : (MODE == 1 ? "mlp_gemm_swiglu_bwd" : "qkv_gemm_rope"));
+  const char* name = MODE == 0 ? "mlp_gemm_swiglu_fwd" : (MODE == 1 ? "mlp_gemm_swiglu_bwd" : "qkv_gemm_rope");
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(units * 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // persistent: no more pairs than can be resident at once
+    int resident = 0;
+    if (cudaOccupancyMaxActiveClusters(&resident, kern, &cfg) == cudaSuccess && resident > 0 && resident < units)
+      cfg.gridDim = dim3((unsigned)(resident * 2));
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, prm);
+    if (err != cudaSuccess) {
+      set_last_error(name, err);
+      return MT_ERR_LAUNCH;
+    }
+  } else {
+    kern<<<units, kThreads, C::SMEM, stream>>>(prm);
+  }
+  return check_launch(name);
 }
+
+template <int MODE>
+int launch(GemmParams& prm, int dtype, int64_t M, int64_t K, int64_t N, cudaStream_t stream) {
+  if constexpr (MODE == 0)
+    if (use_pair(MODE, M)) return launch_impl<MODE, true>(prm, dtype, M, K, N, stream);
+  return launch_impl<MODE, false>(prm, dtype, M, K, N, stream);
+}
+// B's tensor map box holds the rows one CTA stages: 256, or 128 for a pair.
+uint32_t b_box_rows(int MODE, int64_t M) { return use_pair(MODE, M) ? kBN / 2 : kBN; }
 
 }  // namespace
 }  // namespace mt
@@ -459,7 +580,8 @@ extern "C" int mt_swiglu_gemm_fwd(const void* x, const void* w13, void* gu, void
   GemmParams prm;
   prm.status = status;
   if ((st = map_2d(&prm.tm_a, dtype, x, K, M, K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
-  if ((st = map_2d(&prm.tm_b, dtype, w13, K, 2 * I, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w13, K, 2 * I, K, kBK, b_box_rows(0, M), CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK)
+    return st;
   if ((st = map_2d(&prm.tm_gu, dtype, gu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   if ((st = map_2d(&prm.tm_out, dtype, y, I, M, I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   return launch<0>(prm, dtype, M, K, 2 * I, static_cast<cudaStream_t>(stream));
@@ -476,7 +598,8 @@ extern "C" int mt_swiglu_gemm_bwd(const void* dout, const void* w2t, const void*
   GemmParams prm;
   prm.status = status;
   if ((st = map_2d(&prm.tm_a, dtype, dout, H, M, H, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
-  if ((st = map_2d(&prm.tm_b, dtype, w2t, H, I, H, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w2t, H, I, H, kBK, b_box_rows(1, M), CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK)
+    return st;
   if ((st = map_2d(&prm.tm_gu, dtype, gu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   if ((st = map_2d(&prm.tm_out, dtype, dgu, 2 * I, M, 2 * I, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   return launch<1>(prm, dtype, M, H, I, static_cast<cudaStream_t>(stream));
@@ -508,7 +631,7 @@ extern "C" int mt_qkv_rope_gemm(const void* x, const void* w, void* qkv, const v
   prm.head_dim = (int)head_dim;
   prm.rot_cols = (int)rot_cols;
   if ((st = map_2d(&prm.tm_a, dtype, x, K, M, K, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
-  if ((st = map_2d(&prm.tm_b, dtype, w, K, N, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
+  if ((st = map_2d(&prm.tm_b, dtype, w, K, N, K, kBK, b_box_rows(2, M), CU_TENSOR_MAP_SWIZZLE_128B)) != MT_OK) return st;
   if ((st = map_2d(&prm.tm_out, dtype, qkv, N, M, N, kEC, kBM, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK) return st;
   return launch<2>(prm, dtype, M, K, N, static_cast<cudaStream_t>(stream));
 }
