@@ -23,7 +23,7 @@
 //   * Per slot s: S = Q K^T (M=128, N=128, K=D) accumulates in TMEM columns
 //     [256s, 256s+128); O += P V (M=128, N=D, K=128) in [256s+128, 256s+128+D);
 //     P lives in [256s+192, 256s+256).
-//   * Q/K/V tiles arrive by TMA (no multicast) in the 128B (D=64) or 64B (D=32)
+//   * Q/K/V tiles arrive by TMA (one copy per CTA) in the 128B (D=64) or 64B (D=32)
 //     swizzle that the UMMA shared-memory descriptors expect; V is consumed
 //     MN-major so it needs no transpose.  K/V are double-buffered.
 //   * P is rounded to the input dtype (as the reference does before its PV

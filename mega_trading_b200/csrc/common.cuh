@@ -335,7 +335,7 @@ __device__ __forceinline__ bool bar_all(bool v, int id, int count) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA (every load fills the issuing CTA's own shared memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -448,7 +448,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
 // leader): the shared::cluster window puts the odd CTA one bit-24 step above.
 __device__ __forceinline__ uint32_t leader_addr(const void* bar) { return smem_u32(bar) & 0xFEFFFFFFu; }
 // TMA tile load into this CTA's shared memory whose completion (bytes) is
-// counted on the pair leader's mbarrier (address from leader_addr).  No multicast.
+// counted on the pair leader's mbarrier (address from leader_addr).
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t leader_bar, int c0,
                                                  int c1) {
   asm volatile(

@@ -41,9 +41,9 @@
 // 48 KB: a single CTA streaming a whole 128 x 256 tile needs ~1.5x the
 // shared-memory bandwidth the tensor core leaves for it), and holds its 128
 // accumulator rows in its own TMEM.  Both CTAs' stage loads (cta_group::2
-// TMA, no multicast) complete on the even CTA's full barrier, which expects
+// TMA, each into its own CTA's memory) complete on the even CTA's full barrier, which expects
 // both CTAs' bytes; the even CTA issues the MMAs and commits to both CTAs'
-// empty / accumulator barriers (multicast commit); both epilogues release the
+// empty / accumulator barriers (one commit with a two-CTA mask); both epilogues release the
 // accumulator to the even CTA.  Before teardown the odd CTA waits (bounded)
 // for the release of every stage it loaded, which the even CTA's MMAs can
 // only signal after those bytes landed.  (MODE 1 is bound by its gate/up HBM
