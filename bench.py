@@ -46,7 +46,7 @@ CPU_SAMPLE_SEQS = 1
 # B=128, Hq=12, Hkv=4, T=2048, D=64 (profiles/attention_bwd_config3_layer.txt);
 # traffic grows with the batch, so a launch of B sequences moves B/128 times this.
 # Keyed by the workload whose shape it was captured on.
-ATTN_BWD_DRAM_BYTES = {"gqa12": (1_904_392_192 + 1_030_479_616, 128)}
+ATTN_BWD_DRAM_BYTES = {"gqa12": (1_904_345_088 + 1_028_964_352, 128)}
 
 
 def _ref_config(name: str):
