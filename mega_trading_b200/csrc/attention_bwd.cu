@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           const int col0 = wg * 64 + c * 16;
           const int lim = key - (qi * kBQ + col0);  // column i is masked when i < lim (key > query)
           float lv[16], dlv[16];
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; i += 4) {
             const float4 a = *reinterpret_cast<const float4*>(lse + col0 + i);
             const float4 d = *reinterpret_cast<const float4*>(dl + col0 + i);
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
             dlv[i] = d.x; dlv[i + 1] = d.y; dlv[i + 2] = d.z; dlv[i + 3] = d.w;
           }
           const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; i += 2) {
             // P = exp2(s * scale * log2e - lse * log2e), dS = P (dP - delta), two lanes per instruction
             const float2 x = fma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sc2,
@@ -582,12 +582,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           ok = false;
           break;
         }
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int col0 = wg * 64 + c * 32;
           uint8_t* db = sDS + (col0 >> 6) * (128 * 128) + r * 128;
           const int ch0 = (col0 & 63) >> 3;
-  #pragma unroll
+#pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int off = ((ch0 + q) ^ (r & 7)) * 16;
             *reinterpret_cast<uint4*>(db + off) = make_uint4(dk[c][q * 4], dk[c][q * 4 + 1], dk[c][q * 4 + 2], dk[c][q * 4 + 3]);
@@ -629,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
                      int64_t(key) * p.dvs[2] + wg * kCols;
           T* dkrow = static_cast<T*>(p.dk) + int64_t(w.b) * p.dks[0] + int64_t(w.hk) * p.dks[1] +
                      int64_t(key) * p.dks[2] + wg * kCols;
-  #pragma unroll
+#pragma unroll
           for (int q = 0; q < kCols / 8; ++q) {
             uint4 a, c;
             a.x = pack2<T>(__uint_as_float(vv[q * 8 + 0]), __uint_as_float(vv[q * 8 + 1]));
@@ -637,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
             a.z = pack2<T>(__uint_as_float(vv[q * 8 + 4]), __uint_as_float(vv[q * 8 + 5]));
             a.w = pack2<T>(__uint_as_float(vv[q * 8 + 6]), __uint_as_float(vv[q * 8 + 7]));
             float g[8];
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 8; ++i) g[i] = __uint_as_float(kv[q * 8 + i]) * p.scale;
             if (p.rope_cos != nullptr) rope_back8<T>(g, p.rope_cos, p.rope_sin, p.rope_ld, key, (wg * kCols + q * 8) / 2);
             c.x = pack2<T>(g[0], g[1]);
