@@ -78,6 +78,12 @@ class PackedWeights:
         self._versions: list[int] = []
         self._owner = None  # weak reference to the AdamWShadow that keeps this copy current
 
+    def __getstate__(self):
+        # a copy (deepcopy, pickle) is owned by no optimizer and rebuilds its tensor
+        state = dict(self.__dict__)
+        state.update(tensor=None, _versions=[], _owner=None)
+        return state
+
     # -------- layout
     def parts(self) -> list[_Part]:
         out = []

@@ -207,3 +207,21 @@ def test_fused_adamw_refuses_cpu_parameters():
         opt.step()
     with pytest.raises(ValueError):
         AdamWShadow([w], lr=-1.0)
+
+
+def test_copied_packed_weights_are_not_owned():
+    import copy
+
+    from mega_trading_b200.optim import AdamWShadow, PackedWeights
+
+    lin = torch.nn.Linear(8, 4, bias=False)
+    pw = PackedWeights([lin.weight])
+    lin.__dict__["_w_bf16"] = pw
+    opt = AdamWShadow(lin.parameters(), packed=[pw])
+    pw.get()
+    clone = copy.deepcopy(lin)
+    cpw = clone.__dict__["_w_bf16"]
+    assert pw.owned and not cpw.owned and cpw.tensor is None
+    assert cpw.params[0] is clone.weight  # the copy follows the copied parameter
+    assert torch.equal(cpw.get(), clone.weight.detach().to(torch.bfloat16))
+    del opt
