@@ -83,9 +83,11 @@ def test_fused_blocks_reject_bad_input(cuda_device):
 
 
 @pytest.mark.parametrize("M,H,I,seed", [(4096, 768, 2048, 61), (300, 256, 512, 62), (1, 768, 256, 63),
-                                        (1000, 64, 768, 64), (513, 200, 256, 66)])
+                                        (1000, 64, 768, 64), (513, 200, 256, 66), (129, 256, 256, 67),
+                                        (256, 128, 512, 68)])
 def test_swiglu_mlp_matches_oracle(cuda_device, M, H, I, seed):
-    """Fused SwiGLU MLP (gate inside the tcgen05 GEMM epilogues) vs the fp32 oracle."""
+    """Fused SwiGLU MLP (gate inside the tcgen05 GEMM epilogues) vs the fp32 oracle.  M > 128 runs
+    the gate/up GEMM on CTA pairs (M = 129: the odd CTA's rows lie past M; 256: one pair tile)."""
     from mega_trading_b200.kernels.fused_blocks import interleave_gate_up, swiglu_mlp
 
     g = torch.Generator().manual_seed(seed)
