@@ -192,7 +192,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": wl["metric"], "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": 1000 * el / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic composite-token streams",
-        "config": {"workload": wl["workload"], "model": wl["model"],
+        "config": {"workload": wl["workload"], "architecture": wl["model"],
                    "global_batch": CPU_SAMPLE_SEQS, "seq_len": SEQ, "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"{CPU_SAMPLE_SEQS} x {SEQ}-token sequence per step (bounded sample of the "
@@ -344,7 +344,7 @@ def main(argv: list[str] | None = None) -> int:
             "data": "synthetic composite-token streams (seeded, BASELINE distribution), generated on device",
             "config": {
                 "workload": wl["workload"],
-                "model": wl["model"] + " (dropout 0, tied embeddings)",
+                "architecture": wl["model"] + " (dropout 0, tied embeddings)",
                 "global_batch": GLOBAL_BATCH, "seq_len": SEQ, "micro_batch": micro,
                 "grad_accum": math.ceil(local_batch / micro), "parallelism": f"dp{world}",
                 "optimizer": "fused AdamW, fp32 master weights",
