@@ -81,6 +81,7 @@ struct GCfg {
   static constexpr int OFF_IN = OFF_OUT + 2 * N_OUT * BOX;
   static constexpr int OFF_BAR = OFF_IN + E * 2 * BOX;
   static constexpr int SMEM = OFF_BAR + 256;
+  static_assert(E <= 8 && 2 * NST + 5 + 8 + E <= 28, "mbarriers overlap the TMEM slot");
   static_assert(SMEM <= 227 * 1024, "more shared memory than one sm_100 CTA may use");
 };
 
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) mlp_gemm_kernel(const __grid_cons
   uint64_t* acc_empty = acc_full + 2;        // [2]
   uint64_t* fin = acc_full + 4;
   uint64_t* in_full = fin + 1;               // [E]
-  uint64_t* in_empty = in_full + 4;          // [E]
+  uint64_t* in_empty = in_full + 8;          // [E], E <= 8
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 29);
 
