@@ -225,3 +225,22 @@ def test_copied_packed_weights_are_not_owned():
     assert cpw.params[0] is clone.weight  # the copy follows the copied parameter
     assert torch.equal(cpw.get(), clone.weight.detach().to(torch.bfloat16))
     del opt
+
+
+def test_bench_workloads_match_the_model_configs():
+    """Both bench workloads are BASELINE configs 3 and 4, and the CPU reference arm builds
+    the oracle model with the same fields as the product's."""
+    import bench
+
+    from mega_trading_b200.model import CONFIGS
+
+    assert set(bench.WORKLOADS) == {"gqa12", "large24"}
+    w3, w4 = bench.WORKLOADS["gqa12"], bench.WORKLOADS["large24"]
+    assert (w3["global_batch"], w3["seq"]) == (256, 2048) and (w4["global_batch"], w4["seq"]) == (128, 4096)
+    for name in bench.WORKLOADS:
+        ref = bench._ref_config(name)
+        cfg = CONFIGS[name]
+        for field in ("vocab_size", "hidden_dim", "layers", "attention_heads", "kv_heads", "intermediate_dim",
+                      "rope_theta", "norm_eps", "block_size"):
+            assert getattr(ref, field) == getattr(cfg, field), (name, field)
+        assert cfg.block_size >= bench.WORKLOADS[name]["seq"]
