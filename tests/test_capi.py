@@ -63,6 +63,13 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.mt_fused_ce_workspace_bytes(1024, 21504) > 1024 * 4
     assert lib.mt_attention_bwd_workspace_bytes(2, 4, 130, 64) >= 2 * 4 * 256 * 64 * 4
     assert lib.mt_attention_fwd_workspace_bytes(2, 4, 130, 64) >= 4
+    # the forward's work-counter workspace: missing, misaligned or too small
+    fake = ctypes.c_void_p(4096)
+    st16 = _lib.i64_array([4 * 8 * 64, 8 * 64, 64, 1])
+    args = (fake, fake, fake, fake, fake, 2, 1, 4, 4, 8, 64, st16, st16, st16, st16, 0.125)
+    assert lib.mt_attention_fwd(*args, None, 256, fake, None) == 7
+    assert lib.mt_attention_fwd(*args, ctypes.c_void_p(4100), 256, fake, None) == 7
+    assert lib.mt_attention_fwd(*args, fake, 8, fake, None) == 7
     # fused AdamW: nothing to do, unsupported copy dtype, missing table
     assert lib.mt_adamw_step(None, 0, 0, 2, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None) == 0
     assert lib.mt_adamw_step(ctypes.c_void_p(16), 1, 8, 0, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None) == 2
