@@ -50,7 +50,7 @@ constexpr int kRing = 4;       // work items announced ahead by the producer war
 // Of every 8 pairs of scores, kPolyPairs take the polynomial exp2 on the FMA
 // pipe and the rest the MUFU ex2 (16 per clock per SM), the forward's
 // bottleneck at D=64: measured best at 2 (654 vs 646 at 1, 628 at 3 TFLOP/s
-// at T=4096).
+// at T=4096; 676 vs 621 / 628 at B=128, Hq 12, T=2048, and best at T=1024).
 constexpr int kPolyPairs = 2;
 constexpr uint32_t kKernelId = 1;
 
