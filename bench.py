@@ -255,8 +255,13 @@ def main(argv: list[str] | None = None) -> int:
     with ClockSampler(local) as clocks:
         clocks.mark()
         start.record(stream)
+        step_ev = []
         for _ in range(args.steps):
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(stream)
             loss = trainer.step(ids, labels)
+            ev[1].record(stream)
+            step_ev.append(ev)
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -281,10 +286,15 @@ def main(argv: list[str] | None = None) -> int:
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
+    e2e_ev = []
     for _ in range(e2e_steps):
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record(stream)
         dev_tokens.copy_(host, non_blocking=True)
         loss = trainer.step(dev_tokens[:, :-1], dev_tokens[:, 1:])
         loss_host.copy_(loss, non_blocking=True)
+        ev[1].record(stream)
+        e2e_ev.append(ev)
     e_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -292,6 +302,11 @@ def main(argv: list[str] | None = None) -> int:
     if world > 1:
         dist.all_reduce(e_el, op=dist.ReduceOp.MAX)
     e2e_value = tokens_step / (float(e_el.item()) / e2e_steps / 1000.0)
+    status = status or _lib.read_status(device)
+
+    def spread(evs):
+        ms = sorted(a.elapsed_time(b) for a, b in evs)
+        return {"min": ms[0], "median": statistics.median(ms), "max": ms[-1]} if ms else None
 
     # ---------------- roofline of the dominant kernel (attention backward) ----------------
     peaks = _peaks()
@@ -367,7 +382,9 @@ def main(argv: list[str] | None = None) -> int:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": host.numel() * host.element_size(),
                     "d2h_bytes_per_step": 4, "steps": e2e_steps,
-                    "note": "per rank: pinned host tokens copied to HBM and the loss read back every step"},
+                    "note": "per rank: pinned host tokens copied to HBM and the loss read back every step",
+                    "step_ms": spread(e2e_ev)},
+            "step_ms": spread(step_ev),
             "gpu_launches": launches,
             "peak_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
             "device_status": status,
@@ -377,6 +394,9 @@ def main(argv: list[str] | None = None) -> int:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if status:
+        print(f"device status word {status:#x}: {_lib.describe_status(status)}", file=sys.stderr, flush=True)
+        return 1
     return 0
 
 

@@ -62,6 +62,18 @@ MT_API const char* mt_last_error(void);
  *   bit layout: (kernel_id << 16) | wait_site
  */
 
+/* Test hook for the bounded waits (no counterpart in the reference).  Launches
+ * one small kernel that allocates TMEM and waits on an mbarrier through the
+ * same bounded wait the tcgen05 kernels use, with a limit of limit_cycles SM
+ * clock cycles (1 .. 4e9).  complete = 0: nothing arrives, the wait gives up,
+ * the kernel writes (15 << 16) | 1 to *status, frees its TMEM and returns;
+ * complete = 1: the barrier completes and *status is left alone.  Blocks until
+ * the kernel has finished (it synchronises the stream) and returns
+ * MT_ERR_DEVICE_TIMEOUT when *status is nonzero afterwards.  *status must be
+ * zero-initialised device memory. */
+MT_API int mt_debug_wait_timeout(int64_t limit_cycles, int complete, uint32_t* status,
+                                 void* stream);
+
 /* Timing hook (no counterpart in the reference).  Two caller-owned CUDA
  * events (CUevent / cudaEvent_t handles, created by the caller) that the next
  * calls on this host thread record on their stream right before and right
@@ -332,7 +344,10 @@ MT_API int mt_fused_ce_grad_logits(const void* hidden, const void* weight,
  *   p -= lr*wd*p ; m = b1*m + (1-b1)*g ; v = b2*v + (1-b2)*g*g ;
  *   p -= step_size * m / (sqrt(v) / bias_correction2_sqrt + eps)
  * with step_size = lr / (1 - b1^t), bias_correction2_sqrt = sqrt(1 - b2^t)
- * computed by the caller for the tensors' common step t.  Then, when shadow is
+ * computed by the caller for the tensors' common step t.  skip_if_set: NULL,
+ * or a device status word (see above); when it holds a nonzero code at launch
+ * time the kernel changes nothing, so a step whose kernels gave up on a wait
+ * (partial gradients) never reaches the weights.  Then, when shadow is
  * not NULL, the updated value rounded to shadow_dtype (bf16 or fp16) is
  * stored at shadow[(j / shadow_block) * shadow_stride + j % shadow_block] for
  * element j: shadow_block = numel for a contiguous copy; a copy interleaved
@@ -357,7 +372,7 @@ typedef struct MtAdamWTensor {
 MT_API int mt_adamw_step(const MtAdamWTensor* tensors, int n_tensors, int64_t total,
                          int shadow_dtype, float lr, float beta1, float beta2, float eps,
                          float weight_decay, float step_size, float bias_correction2_sqrt,
-                         void* stream);
+                         const uint32_t* skip_if_set, void* stream);
 
 #ifdef __cplusplus
 }

@@ -69,7 +69,8 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "mt_swiglu_packed_fwd": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
     "mt_swiglu_packed_bwd": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
     "mt_adamw_step": (c_int, [c_vp, c_int, c_i64, c_int, c_float, c_float, c_float, c_float, c_float, c_float,
-                              c_float, c_vp]),
+                              c_float, c_vp, c_vp]),
+    "mt_debug_wait_timeout": (c_int, [c_i64, c_int, c_vp, c_vp]),
     "mt_attention_fwd_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
     "mt_attention_fwd": (
         c_int,
@@ -177,6 +178,69 @@ def read_status(device: torch.device) -> int:
     if v:
         t.zero_()
     return v
+
+
+# kernel ids of the status word's high half (the kKernelId constants in csrc/)
+KERNEL_NAMES = {1: "attention forward", 2: "attention backward", 3: "fused cross-entropy", 4: "fused cross-entropy",
+                6: "projection GEMM", 15: "wait probe"}
+
+
+def describe_status(code: int) -> str:
+    """Text for a nonzero device status word: which kernel gave up and where."""
+    kid, site = code >> 16, code & 0xFFFF
+    if site == 0xEEEE:
+        return f"{KERNEL_NAMES.get(kid, f'kernel {kid}')}: a target label is out of range [0, vocab)"
+    if site == 0xFFFF:
+        return f"{KERNEL_NAMES.get(kid, f'kernel {kid}')}: dynamic shared memory not 1024-byte aligned"
+    return f"{KERNEL_NAMES.get(kid, f'kernel {kid}')}: bounded device wait {site} gave up (status {code:#x})"
+
+
+def check_status(device: torch.device) -> None:
+    """Raise :class:`B200KernelError` if a kernel on ``device`` reported an error through the
+    status word since the last check (synchronises the device; clears the word)."""
+    v = read_status(device)
+    if v:
+        raise B200KernelError(f"device error reported by the sm_100a kernels: {describe_status(v)}")
+
+
+class StatusMonitor:
+    """Deferred check of the device status word that never stalls the launch queue.
+
+    ``poll()`` (once per training step) queues an asynchronous copy of the word
+    into pinned host memory behind the step's kernels, then inspects every earlier
+    copy that the device has finished; it blocks only when more than ``depth``
+    copies are outstanding.  A nonzero word raises :class:`B200KernelError` at the
+    first poll after the device wrote it (at most ``depth`` steps late)."""
+
+    def __init__(self, device: torch.device, depth: int = 2) -> None:
+        self.device = device
+        self.depth = max(1, int(depth))
+        self.pending: list[tuple[torch.Tensor, torch.cuda.Event]] = []
+
+    def _inspect(self, host: torch.Tensor) -> None:
+        v = int(host[0])
+        if v:
+            self.pending.clear()
+            status_word(self.device).zero_()
+            raise B200KernelError(f"device error reported by the sm_100a kernels: {describe_status(v)}")
+
+    def poll(self) -> None:
+        host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        host.copy_(status_word(self.device), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.pending.append((host, ev))
+        while self.pending and (self.pending[0][1].query() or len(self.pending) > self.depth):
+            h, e = self.pending.pop(0)
+            e.synchronize()
+            self._inspect(h)
+
+    def flush(self) -> None:
+        """Wait for every queued copy and raise if any holds an error."""
+        while self.pending:
+            h, e = self.pending.pop(0)
+            e.synchronize()
+            self._inspect(h)
 
 
 def require_cuda_sm100(t: torch.Tensor, op: str) -> None:

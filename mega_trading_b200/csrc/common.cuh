@@ -276,6 +276,7 @@ struct WaitCtx {
   uint32_t* status;        // device status word (global)
   volatile int* abort_flag;  // shared-memory abort flag of this CTA
   uint32_t kernel_id;
+  long long limit = kWaitCycles;  // SM clock cycles before a wait gives up
 };
 
 __device__ __forceinline__ bool wait_bounded(const WaitCtx& ctx, uint64_t* bar, uint32_t parity, uint32_t site) {
@@ -284,7 +285,7 @@ __device__ __forceinline__ bool wait_bounded(const WaitCtx& ctx, uint64_t* bar, 
   while (true) {
     if (*ctx.abort_flag) return false;
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > ctx.limit) {
       atomicCAS(ctx.status, 0u, (ctx.kernel_id << 16) | site);
       *ctx.abort_flag = 1;
       return false;
@@ -300,7 +301,7 @@ __device__ __forceinline__ bool wait_bounded_cluster(const WaitCtx& ctx, uint64_
   while (true) {
     if (*ctx.abort_flag) return false;
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > ctx.limit) {
       atomicCAS(ctx.status, 0u, (ctx.kernel_id << 16) | site);
       *ctx.abort_flag = 1;
       return false;
@@ -313,7 +314,7 @@ __device__ __forceinline__ bool wait_bounded_cluster(const WaitCtx& ctx, uint64_
 __device__ __forceinline__ bool wait_drain(const WaitCtx& ctx, uint64_t* bar, uint32_t parity, uint32_t site) {
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > ctx.limit) {
       atomicCAS(ctx.status, 0u, (ctx.kernel_id << 16) | site);
       return false;
     }

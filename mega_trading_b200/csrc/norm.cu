@@ -694,7 +694,27 @@ int noalloc_scratch(const void* any_device_ptr, float** out) {
     set_last_error("cudaGetDevice", err);
     return MT_ERR_LAUNCH;
   }
-  if (dev < 0 || dev >= kMaxNoAllocDevices) return MT_ERR_INVALID_ARGUMENT;
+  if (dev < 0 || dev >= kMaxNoAllocDevices) {
+    set_last_error_text("mt_rms_norm_bwd_noalloc: device index beyond the library's per-device table (64)");
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  // The scratch address is per device: the tensors must live on the current
+  // device, or the kernel would run there with another device's array.
+  cudaPointerAttributes attr;
+  err = cudaPointerGetAttributes(&attr, any_device_ptr);
+  if (err != cudaSuccess) {
+    set_last_error("mt_rms_norm_bwd_noalloc: cudaPointerGetAttributes(x)", err);
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  if (attr.type != cudaMemoryTypeDevice) {
+    set_last_error_text("mt_rms_norm_bwd_noalloc: x is not device memory");
+    return MT_ERR_INVALID_ARGUMENT;
+  }
+  if (attr.device != dev) {
+    set_last_error_text("mt_rms_norm_bwd_noalloc: x lives on another device than the current one; "
+                        "make the tensors' device current before the call");
+    return MT_ERR_INVALID_ARGUMENT;
+  }
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_addr[dev] == nullptr) {
     void* ptr = nullptr;

@@ -32,6 +32,7 @@ struct AdamWArgs {
   float eps;
   float step_size;   // lr / (1 - beta1^t)
   float bc2_sqrt;    // sqrt(1 - beta2^t)
+  const uint32_t* guard;  // device status word: nonzero -> leave everything untouched
 };
 
 __device__ __forceinline__ int find_tensor(const MtAdamWTensor* __restrict__ t, int n, int64_t i) {
@@ -71,6 +72,9 @@ __global__ void __launch_bounds__(kOptThreads) adamw_kernel(const MtAdamWTensor*
                                                             int64_t total, AdamWArgs a) {
   const int64_t base = int64_t(blockIdx.x) * kOptChunk;
   if (base >= total) return;
+  // a kernel of this step reported a device error: its gradients may be
+  // partial, so no weight, moment or copy is changed
+  if (a.guard != nullptr && *a.guard != 0u) return;
   int t = find_tensor(tab, n_tensors, base);
   const MtAdamWTensor d = tab[t];
   if (base + kOptChunk <= d.offset + d.numel) {
@@ -119,7 +123,7 @@ using namespace mt;
 
 extern "C" int mt_adamw_step(const MtAdamWTensor* tensors, int n_tensors, int64_t total, int shadow_dtype,
                              float lr, float beta1, float beta2, float eps, float weight_decay, float step_size,
-                             float bias_correction2_sqrt, void* stream) {
+                             float bias_correction2_sqrt, const uint32_t* skip_if_set, void* stream) {
   if (n_tensors < 0 || total < 0) return MT_ERR_INVALID_ARGUMENT;
   if (n_tensors == 0 || total == 0) return MT_OK;
   if (tensors == nullptr) return MT_ERR_INVALID_ARGUMENT;
@@ -134,6 +138,7 @@ extern "C" int mt_adamw_step(const MtAdamWTensor* tensors, int n_tensors, int64_
   a.eps = eps;
   a.step_size = step_size;
   a.bc2_sqrt = bias_correction2_sqrt;
+  a.guard = skip_if_set;
   const int64_t blocks = (total + kOptChunk - 1) / kOptChunk;
   if (blocks > 0x7fffffff) return MT_ERR_INVALID_ARGUMENT;
   auto s = static_cast<cudaStream_t>(stream);

@@ -11,6 +11,7 @@ materialises fp32 T x T tensors, ``triton_attention.py:85-111``).
 from __future__ import annotations
 
 import math
+import warnings
 
 import torch
 
@@ -76,11 +77,26 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None, ro
     return dq, dk, dv
 
 
+#: number of inputs whose layout the TMA tensor maps cannot take (inner stride
+#: not 1, an outer stride not a multiple of 8 elements, or a base address not
+#: 16-byte aligned) and which were therefore copied to a contiguous tensor
+layout_copies = 0
+
+
 def _aligned_view(t: torch.Tensor) -> torch.Tensor:
-    """Return ``t`` if the kernels accept its layout, else a contiguous copy."""
+    """Return ``t`` if the kernels accept its layout, else a contiguous copy
+    (counted in ``layout_copies``; the first one also warns)."""
+    global layout_copies
     s = t.stride()
     ok = s[3] == 1 and all(x % 8 == 0 and x > 0 for x in s[:3]) and t.data_ptr() % 16 == 0
-    return t if ok else t.contiguous()
+    if ok:
+        return t
+    if layout_copies == 0:
+        warnings.warn(f"triton_attention: an input with strides {tuple(s)} is copied to a contiguous tensor "
+                      "(the sm_100a kernels read unit inner stride, outer strides that are multiples of 8 "
+                      "elements and 16-byte aligned bases); see layout_copies", stacklevel=4)
+    layout_copies += 1
+    return t.contiguous()
 
 
 class _CausalAttention(torch.autograd.Function):

@@ -242,6 +242,6 @@ class AdamWShadow(torch.optim.Optimizer):
         bc2 = 1.0 - beta2 ** t
         st = lib.mt_adamw_step(self._table.data_ptr(), len(rows), total, _lib.dtype_code(_BF16), float(lr),
                                float(beta1), float(beta2), float(eps), float(wd), float(lr / bc1),
-                               float(math.sqrt(bc2)), _lib.stream_ptr(dev))
+                               float(math.sqrt(bc2)), _lib.status_word(dev).data_ptr(), _lib.stream_ptr(dev))
         _lib.check(st, "adamw step")
         _lib.count(1)

@@ -20,6 +20,7 @@ import os
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .model import ModelConfig, TradingModelB200
 from .optim import AdamWShadow
 
@@ -74,6 +75,17 @@ class Trainer:
                 self.model.parameters(), lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=weight_decay,
                 fused=device.type == "cuda",
             )
+        # device status word of the bounded waits and the label check: the fused
+        # AdamW leaves the weights alone when it is set, and every step polls it
+        # without stalling (an error raises at most two steps later)
+        self.monitor = _lib.StatusMonitor(device) if device.type == "cuda" else None
+
+    def check_status(self) -> None:
+        """Wait for the device and raise :class:`~mega_trading_b200._lib.B200KernelError` if a
+        kernel of an earlier step reported an error."""
+        if self.monitor is not None:
+            self.monitor.flush()
+            _lib.check_status(self.device)
 
     def step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         """One optimizer step over this rank's ``[B, T]`` batch; returns the mean loss (device scalar,
@@ -92,4 +104,6 @@ class Trainer:
             total += loss.detach() * frac
         self.opt.step()
         self.opt.zero_grad(set_to_none=self.world == 1)
+        if self.monitor is not None:
+            self.monitor.poll()
         return total

@@ -113,6 +113,43 @@ def linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, labels: tor
     return F.cross_entropy(F.linear(hidden, weight), labels, ignore_index=ignore_index)
 
 
+@torch.no_grad()
+def linear_cross_entropy_grads(hidden: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor,
+                               ignore_index: int = -100, grad_output: float = 1.0,
+                               chunk_rows: int = 8192) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``(loss, d_hidden, d_weight)`` of :func:`linear_cross_entropy` in fp32, computed
+    analytically over row chunks on the inputs' device: the reference's chunked
+    recipe (triton_ops.py:359-389: logits of one chunk, softmax minus one-hot of
+    the target scaled by 1/n_valid, ``grad_hidden = dZ W``, ``grad_weight += dZ^T H``)
+    with the loss of triton_ops.py:99-112 (mean over non-ignored rows, 0 when
+    every row is ignored).  For sizes whose full [N, V] logits do not fit."""
+    h = hidden.float()
+    w = weight.float()
+    valid = labels != ignore_index
+    n_valid = int(valid.sum().item())
+    dh = torch.zeros_like(h)
+    dw = torch.zeros_like(w)
+    if n_valid == 0:
+        return torch.zeros((), dtype=torch.float32, device=h.device), dh, dw
+    scale = grad_output / n_valid
+    total = torch.zeros((), dtype=torch.float64, device=h.device)
+    for lo in range(0, h.shape[0], chunk_rows):
+        hi = min(h.shape[0], lo + chunk_rows)
+        z = h[lo:hi] @ w.t()
+        lse = torch.logsumexp(z, dim=-1)
+        lab = labels[lo:hi]
+        ok = valid[lo:hi]
+        safe = torch.where(ok, lab, torch.zeros_like(lab)).long()
+        zy = z.gather(1, safe[:, None]).squeeze(1)
+        total += ((lse - zy) * ok).double().sum()
+        dz = torch.softmax(z, dim=-1)
+        dz[torch.arange(hi - lo, device=z.device), safe] -= 1.0
+        dz *= (ok.float() * scale)[:, None]
+        dh[lo:hi] = dz @ w
+        dw += dz.t() @ h[lo:hi]
+    return (total / n_valid).float(), dh, dw
+
+
 def max_rel_error(actual: torch.Tensor, expected: torch.Tensor) -> float:
     """Normwise max relative error ``max|a - b| / max|b|`` (the BASELINE metric)."""
     a = _f32(actual)

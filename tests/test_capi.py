@@ -71,9 +71,9 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.mt_attention_fwd(*args, ctypes.c_void_p(4100), 256, fake, None) == 7
     assert lib.mt_attention_fwd(*args, fake, 8, fake, None) == 7
     # fused AdamW: nothing to do, unsupported copy dtype, missing table
-    assert lib.mt_adamw_step(None, 0, 0, 2, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None) == 0
-    assert lib.mt_adamw_step(ctypes.c_void_p(16), 1, 8, 0, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None) == 2
-    assert lib.mt_adamw_step(None, 1, 8, 2, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None) == 1
+    assert lib.mt_adamw_step(None, 0, 0, 2, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None, None) == 0
+    assert lib.mt_adamw_step(ctypes.c_void_p(16), 1, 8, 0, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None, None) == 2
+    assert lib.mt_adamw_step(None, 1, 8, 2, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1e-3, 1.0, None, None) == 1
 
 
 @pytest.mark.parametrize("name", ["mt_rms_norm_fwd", "mt_attention_fwd", "mt_fused_ce_fwd"])

@@ -48,7 +48,7 @@ def test_model_loss_and_grads_match_oracle(cuda_device, cfg_kwargs, batch, seq):
     lo, _ = o.forward_with_loss(ids, labels)
     lo.backward()
     rel = abs(float(loss.detach()) - float(lo.detach())) / float(lo.detach())
-    assert rel < 2e-3, f"loss {float(loss):.6f} vs oracle {float(lo):.6f}"
+    assert rel < 2e-3, f"loss {float(loss.detach()):.6f} vs oracle {float(lo.detach()):.6f}"
     ours = dict(m.named_parameters())
     worst = 0.0
     for name, p in o.named_parameters():
@@ -68,8 +68,8 @@ def test_return_logits_path(cuda_device):
         fused, none = m.forward_with_loss(ids.to(cuda_device), labels.to(cuda_device))
         lo, _ = o.forward_with_loss(ids, labels)
     assert none is None and logits.shape == (1, 128, 21504)
-    assert abs(float(loss) - float(lo)) / float(lo) < 2e-3
-    assert abs(float(fused) - float(loss)) / float(loss) < 2e-3
+    assert abs(float(loss.detach()) - float(lo.detach())) / float(lo.detach()) < 2e-3
+    assert abs(float(fused.detach()) - float(loss.detach())) / float(loss.detach()) < 2e-3
 
 
 def test_trainer_steps_reduce_loss(cuda_device):

@@ -96,6 +96,17 @@ def test_fused_ce_golden(key):
     assert torch.allclose(w.grad, g["dw"], **TOL)
 
 
+@pytest.mark.parametrize("key", ["fused_ce", "fused_ce_all_ignored"])
+@pytest.mark.parametrize("chunk", [7, 64, 8192])
+def test_chunked_ce_gradients_golden(key, chunk):
+    """The analytic chunked restatement (used at config-2 sizes) against the reference's outputs."""
+    g = GOLDEN[key]
+    loss, dh, dw = O.linear_cross_entropy_grads(g["hidden"], g["weight"], g["labels"], -100, chunk_rows=chunk)
+    assert torch.allclose(loss, g["loss"].float(), **TOL)
+    assert torch.allclose(dh, g["dh"], **TOL)
+    assert torch.allclose(dw, g["dw"], **TOL)
+
+
 def test_model_golden():
     g = GOLDEN["model"]
     c = g["config"]
