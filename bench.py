@@ -332,10 +332,13 @@ def main(argv: list[str] | None = None) -> int:
         for key in (name, name + "_kernel"):
             if key in kern:
                 kernels[key]["tflops"] = fl / (kern[key][1] / 1000.0) / 1e12
+    # algorithmic CE work: forward 2NHV (logits), backward 4NHV (dH and dW); the
+    # backward also recomputes the logits twice (4NHV more), not counted here
     ce_flops = 2.0 * B * SEQ * cfg.hidden_dim * cfg.vocab_size
-    for name in ("fused_ce_fwd", "fused_ce_grad_logits"):
+    for name, mult in (("fused_ce_fwd", 1.0), ("fused_ce_bwd", 2.0)):
         if name in kern:
-            kernels[name]["tflops"] = ce_flops / (kern[name][1] / 1000.0) / 1e12
+            kernels[name]["tflops"] = mult * ce_flops / (kern[name][1] / 1000.0) / 1e12
+            kernels[name]["tflops_executed"] = (1.0 if mult == 1.0 else 4.0) * ce_flops / (kern[name][1] / 1e3) / 1e12
     step_flops = cfg.train_flops_per_token(SEQ) * tokens_step
     mfu = step_flops / (ms_step / 1000.0) / 1e12 / (world * peaks["bf16_tflops"])
 

@@ -324,15 +324,24 @@ MT_API int mt_fused_ce_fwd(const void* hidden, const void* weight, const void* l
                            void* workspace, int64_t workspace_bytes, uint32_t* status,
                            void* stream);
 
-/* Backward part 1: dZ = (softmax(hidden W^T) - onehot(label)) / n_valid * grad_out
- * written to dz ([N, dz_ld] row-major, dz_ld >= V, dz_ld % 8 == 0) in the input
- * dtype; the logits are recomputed on chip.  grad_out: device fp32 scalar.
- * The caller finishes with dH = dZ W and dW = dZ^T hidden. */
-MT_API int mt_fused_ce_grad_logits(const void* hidden, const void* weight,
-                                   const void* labels, int labels_i64,
-                                   int64_t ignore_index, int dtype, int64_t N, int64_t V,
-                                   int64_t K, const float* lse2_scal, const float* grad_out,
-                                   void* dz, int64_t dz_ld, uint32_t* status, void* stream);
+/* Backward: dhidden = dZ W  [N, K]  and  dweight = dZ^T hidden  [V, K] with
+ *   dZ = (softmax(hidden W^T) - onehot(label)) * grad_out / n_valid
+ * (rows with an ignored or out-of-range label contribute nothing), the
+ * gradients the reference computes chunk by chunk with two library GEMMs over
+ * a materialised logits chunk (kernels/triton_ops.py:359-389).  Here the
+ * logit tiles are recomputed on chip, rounded to dtype and multiplied out of
+ * shared memory: dZ never reaches global memory and the products accumulate
+ * in fp32 (TMEM).  lse2_scal: the forward's lse2_out; grad_out: device fp32
+ * scalar.  dhidden / dweight: contiguous, written completely in dh_dtype /
+ * dw_dtype (MT_F32, MT_BF16 or MT_F16); either may be NULL to skip it.
+ * workspace: mt_fused_ce_bwd_workspace_bytes(N, V, K) bytes, 256-byte aligned. */
+MT_API int64_t mt_fused_ce_bwd_workspace_bytes(int64_t N, int64_t V, int64_t K);
+MT_API int mt_fused_ce_bwd(const void* hidden, const void* weight, const void* labels,
+                           int labels_i64, int64_t ignore_index, int dtype, int64_t N,
+                           int64_t V, int64_t K, const float* lse2_scal, const float* grad_out,
+                           void* dhidden, int dh_dtype, void* dweight, int dw_dtype,
+                           void* workspace, int64_t workspace_bytes, uint32_t* status,
+                           void* stream);
 
 /* ---------------------------------------------------------------------
  * Fused AdamW with 16-bit weight copies   replaces torch.optim.AdamW(fused=True)

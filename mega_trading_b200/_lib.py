@@ -94,9 +94,11 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp],
     ),
-    "mt_fused_ce_grad_logits": (
+    "mt_fused_ce_bwd_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64]),
+    "mt_fused_ce_bwd": (
         c_int,
-        [c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp],
+        [c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_vp,
+         c_i64, c_vp, c_vp],
     ),
 }
 

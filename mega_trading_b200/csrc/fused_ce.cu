@@ -8,26 +8,22 @@
 //   all-ignored -> loss 0), torch path :99-112.
 //
 // B200 design
-//   * ce_logits_kernel<MODE>: a tcgen05 GEMM over tiles of 128 rows x 256
-//     vocab entries (K streamed in 64-wide chunks through a 4-stage TMA ring,
-//     128B swizzle), accumulators double-buffered in TMEM (2 x 256 columns) so
-//     the epilogue of one vocab tile overlaps the MMAs of the next.  The
-//     epilogue reads the logit tile straight out of TMEM:
-//       MODE 0 (forward): online max / sum-exp per row and the target logit;
-//                         the logits never reach global memory.
-//       MODE 1 (backward): recomputes the tile and writes only the logit
-//                         gradient (softmax - onehot) * inv_n * grad_out in
-//                         bf16/fp16 through TMA stores.
-//     The vocabulary is split across CTAs (grid.y) for occupancy; MODE 0
-//     writes per-split partial statistics.
+//   * ce_logits_kernel: a tcgen05 GEMM over tiles of 128 rows x 256 vocab
+//     entries (K streamed in 64-wide chunks through a 4-stage TMA ring, 128B
+//     swizzle), accumulators double-buffered in TMEM (2 x 256 columns) so the
+//     epilogue of one vocab tile overlaps the MMAs of the next.  The epilogue
+//     reads the logit tile straight out of TMEM and keeps an online max /
+//     sum-exp per row and the target logit; the logits never reach global
+//     memory.  The vocabulary is split across CTAs (grid.y) for occupancy;
+//     each split writes partial row statistics.
 //   * ce_merge_kernel: combines the splits into lse per row and the per-row
 //     loss; ce_loss_kernel reduces loss and the valid-row count in one block
 //     (fixed order, no host synchronisation).
-//   * dH = dZ W and dW = dZ^T H are plain GEMMs run by the caller.
+//   * The backward (dH and dW, logits recomputed on chip) is fused_ce_bwd.cu.
 // Warp roles (320 threads): warps 0-7 epilogue in two warpgroups taking
-// alternate 32-column steps of a tile (thread = row = TMEM lane; MODE 0 merges
-// the two warpgroups' row statistics at the end, MODE 1 gives each warpgroup
-// its own staging box), warp 8 TMA producer (+ TMEM allocation), warp 9 MMA.
+// alternate 32-column steps of a tile (thread = row = TMEM lane; the two
+// warpgroups' row statistics are merged at the end), warp 8 TMA producer
+// (+ TMEM allocation), warp 9 MMA.
 #include <cmath>
 #include <type_traits>
 
@@ -43,36 +39,30 @@ constexpr int kThreads = 320;
 constexpr int kEC = 32;  // epilogue columns per step
 constexpr uint32_t kKernelId = 3;
 
-template <int MODE>
 struct CeCfg {
   static constexpr int NST = 4;
   static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
   static constexpr int B_BYTES = kBN * kBK * 2;  // 32 KB
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int OFF_STAGE = 0;
-  // MODE 0: [2][128] x {m, s, z} merge area; MODE 1: one [128][32] 16-bit
-  // box (64B swizzle) per epilogue warpgroup
+  // [2][128] x {m, s, z} merge area of the two epilogue warpgroups
   static constexpr int OFF_OUT = NST * STAGE;
-  static constexpr int OUT_BYTES = MODE == 1 ? 2 * kBM * kEC * 2 : 3 * kBM * 4;
+  static constexpr int OUT_BYTES = 3 * kBM * 4;
   static constexpr int OFF_BAR = OFF_OUT + OUT_BYTES;
   static constexpr int SMEM = OFF_BAR + 256;
 };
 
 struct CeParams {
-  CUtensorMap tm_h, tm_w, tm_dz;
+  CUtensorMap tm_h, tm_w;
   const void* labels;
   int labels_i64;
   int64_t ignore_index;
   int N, V, K, n_vtiles, tiles_per_split;
-  // MODE 0 outputs: per (row, split) partial max (log2 domain), sum, target logit
+  // outputs: per (row, split) partial max (log2 domain), sum, target logit
   float* part_m;
   float* part_s;
   float* part_z;
   int splits;
-  // MODE 1 inputs: lse2 per row (log2 domain), scalars {loss, n_valid, inv_n}
-  const float* lse2;
-  const float* scal;
-  const float* grad_out;  // device scalar multiplying the gradient
   uint32_t* status;
 };
 
@@ -80,9 +70,9 @@ __device__ __forceinline__ int64_t load_label(const CeParams& p, int row) {
   return p.labels_i64 ? static_cast<const int64_t*>(p.labels)[row] : (int64_t) static_cast<const int32_t*>(p.labels)[row];
 }
 
-template <typename T, int MODE>
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_constant__ CeParams p) {
-  using C = CeCfg<MODE>;
+  using C = CeCfg;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = warp_id();
   const int lane = lane_id();
@@ -198,12 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
     float m = -INFINITY, s = 0.f, zy = NAN;
-    float lse2 = 0.f, gscale = 0.f;
-    if constexpr (MODE == 1) {
-      lse2 = in_rows ? p.lse2[row] : 0.f;
-      gscale = valid ? p.scal[2] * p.grad_out[0] : 0.f;
-    }
-    uint8_t* out = smem + C::OFF_OUT + wg * (kBM * kEC * 2);
     bool ok = true;
     for (int t = 0; t < n_vt; ++t) {
       const int buf = t & 1;
@@ -223,74 +207,46 @@ __global__ void __launch_bounds__(kThreads, 1) ce_logits_kernel(const __grid_con
           mbar_arrive(&acc_empty[buf]);
         }
         const int col0 = vbase + c * kEC;
-        if constexpr (MODE == 0) {
-          float x[32];
-          float cm = -INFINITY;
+        float x[32];
+        float cm = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            x[i] = (col0 + i < p.V) ? __uint_as_float(z[i]) * kLog2e : -INFINITY;
-            cm = fmaxf(cm, x[i]);
-          }
-          const float mn = fmaxf(m, cm);
-          float cs = 0.f;
+        for (int i = 0; i < 32; ++i) {
+          x[i] = (col0 + i < p.V) ? __uint_as_float(z[i]) * kLog2e : -INFINITY;
+          cm = fmaxf(cm, x[i]);
+        }
+        const float mn = fmaxf(m, cm);
+        float cs = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) cs += fast_exp2(x[i] - mn);
-          s = (m == -INFINITY ? 0.f : s * fast_exp2(m - mn)) + cs;
-          m = mn;
-          if (valid && label >= col0 && label < col0 + 32) {
-            const int li = int(label - col0);
+        for (int i = 0; i < 32; ++i) cs += fast_exp2(x[i] - mn);
+        s = (m == -INFINITY ? 0.f : s * fast_exp2(m - mn)) + cs;
+        m = mn;
+        if (valid && label >= col0 && label < col0 + 32) {
+          const int li = int(label - col0);
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i == li) zy = __uint_as_float(z[i]);
-          }
-        } else {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = fast_exp2(__uint_as_float(z[i]) * kLog2e - lse2);
-            const float p1 = fast_exp2(__uint_as_float(z[i + 1]) * kLog2e - lse2);
-            pk[i >> 1] = pack2<T>((p0 - ((col0 + i) == label ? 1.f : 0.f)) * gscale,
-                                  (p1 - ((col0 + i + 1) == label ? 1.f : 0.f)) * gscale);
-          }
-          // this warpgroup's previous store must have finished reading its box
-          if (r == 0) bulk_wait_group_read0();
-          named_bar_sync(1 + wg, 128);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(out + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) =
-                make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]);
-          fence_proxy_async_smem();
-          named_bar_sync(1 + wg, 128);
-          if (r == 0) {
-            tma_store_2d(&p.tm_dz, out, col0, row0);
-            bulk_commit_group();
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i == li) zy = __uint_as_float(z[i]);
         }
       }
     }
-    if constexpr (MODE == 0) {
-      // merge the two warpgroups' running statistics of each row
-      float* mg = reinterpret_cast<float*>(smem + C::OFF_OUT);
-      if (wg == 1) {
-        mg[r] = m;
-        mg[128 + r] = s;
-        mg[256 + r] = zy;
+    // merge the two warpgroups' running statistics of each row
+    float* mg = reinterpret_cast<float*>(smem + C::OFF_OUT);
+    if (wg == 1) {
+      mg[r] = m;
+      mg[128 + r] = s;
+      mg[256 + r] = zy;
+    }
+    named_bar_sync(3, 256);
+    if (wg == 0) {
+      const float m1 = mg[r], s1 = mg[128 + r], z1 = mg[256 + r];
+      const float mn = fmaxf(m, m1);
+      const float sm = (m == -INFINITY ? 0.f : s * fast_exp2(m - mn)) + (m1 == -INFINITY ? 0.f : s1 * fast_exp2(m1 - mn));
+      const float zm = isnan(zy) ? z1 : zy;
+      if (ok && in_rows) {
+        const int64_t idx = int64_t(row) * p.splits + split;
+        p.part_m[idx] = mn;
+        p.part_s[idx] = sm;
+        p.part_z[idx] = zm;
       }
-      named_bar_sync(3, 256);
-      if (wg == 0) {
-        const float m1 = mg[r], s1 = mg[128 + r], z1 = mg[256 + r];
-        const float mn = fmaxf(m, m1);
-        const float sm = (m == -INFINITY ? 0.f : s * fast_exp2(m - mn)) + (m1 == -INFINITY ? 0.f : s1 * fast_exp2(m1 - mn));
-        const float zm = isnan(zy) ? z1 : zy;
-        if (ok && in_rows) {
-          const int64_t idx = int64_t(row) * p.splits + split;
-          p.part_m[idx] = mn;
-          p.part_s[idx] = sm;
-          p.part_z[idx] = zm;
-        }
-      }
-    } else {
-      if (r == 0) bulk_wait_group0();
     }
   }
 
@@ -420,15 +376,15 @@ int ce_validate(const void* hidden, const void* weight, const void* labels, int 
   return MT_OK;
 }
 
-template <typename T, int MODE>
+template <typename T>
 int launch_logits(const CeParams& prm, int64_t N, cudaStream_t stream) {
-  using C = CeCfg<MODE>;
-  auto kern = ce_logits_kernel<T, MODE>;
+  using C = CeCfg;
+  auto kern = ce_logits_kernel<T>;
   int st = set_smem_limit((const void*)kern, C::SMEM);
   if (st != MT_OK) return st;
   dim3 grid((unsigned)((N + kBM - 1) / kBM), (unsigned)prm.splits);
   kern<<<grid, kThreads, C::SMEM, stream>>>(prm);
-  return check_launch(MODE == 0 ? "fused_ce_lse" : "fused_ce_grad");
+  return check_launch("fused_ce_lse");
 }
 
 }  // namespace
@@ -474,11 +430,8 @@ extern "C" int mt_fused_ce_fwd(const void* hidden, const void* weight, const voi
   prm.part_m = ws.pm;
   prm.part_s = ws.ps;
   prm.part_z = ws.pz;
-  prm.lse2 = nullptr;
-  prm.scal = nullptr;
-  prm.grad_out = nullptr;
   prm.status = status;
-  st = dtype == MT_BF16 ? launch_logits<__nv_bfloat16, 0>(prm, N, s) : launch_logits<__half, 0>(prm, N, s);
+  st = dtype == MT_BF16 ? launch_logits<__nv_bfloat16>(prm, N, s) : launch_logits<__half>(prm, N, s);
   if (st != MT_OK) return st;
   ce_merge_kernel<<<(unsigned)((N + 255) / 256), 256, 0, s>>>(ws.pm, ws.ps, ws.pz, splits, (int)N, labels, labels_i64,
                                                                ignore_index, (int)V, ws.lse2, ws.row_loss,
@@ -495,44 +448,4 @@ extern "C" int mt_fused_ce_fwd(const void* hidden, const void* weight, const voi
     }
   }
   return MT_OK;
-}
-
-extern "C" int mt_fused_ce_grad_logits(const void* hidden, const void* weight, const void* labels, int labels_i64,
-                                       int64_t ignore_index, int dtype, int64_t N, int64_t V, int64_t K,
-                                       const float* lse2_scal, const float* grad_out, void* dz, int64_t dz_ld,
-                                       uint32_t* status, void* stream) {
-  int st = ce_validate(hidden, weight, labels, dtype, N, V, K);
-  if (st != MT_OK) return st;
-  if (N == 0) return MT_OK;
-  if (lse2_scal == nullptr || grad_out == nullptr || dz == nullptr || status == nullptr) return MT_ERR_INVALID_ARGUMENT;
-  if (dz_ld < V || (dz_ld % 8) != 0 || (reinterpret_cast<uintptr_t>(dz) & 15u)) return MT_ERR_UNSUPPORTED_LAYOUT;
-  if ((st = bind_device_of(hidden)) != MT_OK) return st;
-  if ((st = check_arch()) != MT_OK) return st;
-  CeParams prm;
-  if ((st = ce_maps(prm, hidden, weight, dtype, N, V, K)) != MT_OK) return st;
-  {
-    const CUtensorMapDataType dt =
-        dtype == MT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    uint64_t dims[2] = {(uint64_t)V, (uint64_t)N};
-    uint64_t str[1] = {(uint64_t)dz_ld * 2};
-    uint32_t box[2] = {kEC, kBM};
-    if ((st = encode_tensor_map(&prm.tm_dz, dt, 2, dz, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B)) != MT_OK)
-      return st;
-  }
-  prm.labels = labels;
-  prm.labels_i64 = labels_i64;
-  prm.ignore_index = ignore_index;
-  prm.N = (int)N;
-  prm.V = (int)V;
-  prm.K = (int)K;
-  prm.n_vtiles = (int)((V + kBN - 1) / kBN);
-  prm.splits = ce_splits(N, V);
-  prm.tiles_per_split = (prm.n_vtiles + prm.splits - 1) / prm.splits;
-  prm.part_m = prm.part_s = prm.part_z = nullptr;
-  prm.lse2 = lse2_scal;
-  prm.scal = lse2_scal + N;
-  prm.grad_out = grad_out;
-  prm.status = status;
-  auto s = static_cast<cudaStream_t>(stream);
-  return dtype == MT_BF16 ? launch_logits<__nv_bfloat16, 1>(prm, N, s) : launch_logits<__half, 1>(prm, N, s);
 }

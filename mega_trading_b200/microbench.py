@@ -97,7 +97,9 @@ def ce_cases(dev, iters, profile, n=65536, h=768, v=21504):
     loss = torch.empty((), device=dev)
     lse2 = torch.empty(n + 3, device=dev)
     ws = torch.empty(int(lib.mt_fused_ce_workspace_bytes(n, v)), device=dev, dtype=torch.uint8)
-    dz = torch.empty(n, v, device=dev, dtype=torch.bfloat16)
+    wsb = torch.empty(max(int(lib.mt_fused_ce_bwd_workspace_bytes(n, v, h)), 256), device=dev, dtype=torch.uint8)
+    dh = torch.empty(n, h, device=dev, dtype=torch.bfloat16)
+    dw = torch.empty(v, h, device=dev, dtype=torch.float32)
     one = torch.ones(1, device=dev)
     status = _lib.status_word(dev)
     stream = _lib.stream_ptr(dev)
@@ -107,23 +109,28 @@ def ce_cases(dev, iters, profile, n=65536, h=768, v=21504):
                                        loss.data_ptr(), lse2.data_ptr(), ws.data_ptr(), ws.numel(),
                                        status.data_ptr(), stream), "ce fwd")
 
-    def grad():
-        _lib.check(lib.mt_fused_ce_grad_logits(hid.data_ptr(), w.data_ptr(), lab.data_ptr(), 1, -100, 2, n, v, h,
-                                               lse2.data_ptr(), one.data_ptr(), dz.data_ptr(), v,
-                                               status.data_ptr(), stream), "ce grad")
+    def bwd(want_h=True, want_w=True):
+        _lib.check(lib.mt_fused_ce_bwd(hid.data_ptr(), w.data_ptr(), lab.data_ptr(), 1, -100, 2, n, v, h,
+                                       lse2.data_ptr(), one.data_ptr(), dh.data_ptr() if want_h else None, 2,
+                                       dw.data_ptr() if want_w else None, 0, wsb.data_ptr(), wsb.numel(),
+                                       status.data_ptr(), stream), "ce bwd")
 
     fwd()
     if profile:
         for _ in range(iters):
             fwd()
-            grad()
+            bwd()
         return []
     flops = 2.0 * n * h * v
     ms_f = _time(fwd, iters)
-    ms_g = _time(grad, iters)
+    ms_b = _time(bwd, iters)
+    ms_h = _time(lambda: bwd(True, False), iters)
+    ms_w = _time(lambda: bwd(False, True), iters)
     return [{"op": "fused_ce", "N": n, "H": h, "V": v, "fwd_ms": ms_f, "fwd_tflops": flops / ms_f / 1e9,
-             "grad_logits_ms": ms_g, "grad_logits_tflops": flops / ms_g / 1e9,
-             "grad_logits_bytes_written": n * v * 2}]
+             "bwd_ms": ms_b, "bwd_tflops": 2 * flops / ms_b / 1e9, "bwd_executed_tflops": 4 * flops / ms_b / 1e9,
+             "dh_pass_ms": ms_h, "dh_pass_executed_tflops": 2 * flops / ms_h / 1e9,
+             "dw_pass_ms": ms_w, "dw_pass_executed_tflops": 2 * flops / ms_w / 1e9,
+             "bwd_global_bytes_min": (n * h * 2) * 2 + v * h * 2 + v * h * 4 + n * 16}]
 
 
 def _add_rms_case(dev, g, n, H, res_dtype, iters, profile) -> dict | None:

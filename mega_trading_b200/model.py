@@ -245,10 +245,13 @@ class TradingModelB200(nn.Module):
         if labels.shape != input_ids.shape:
             raise ValueError("labels must match input_ids shape")
         normed = self.hidden_states(input_ids)
-        w_out = _packed(self, "_out_bf16", [self.output.weight]).get()
+        pw_out = _packed(self, "_out_bf16", [self.output.weight])
         if not return_logits:
             flat = normed.reshape(-1, normed.shape[-1])
-            return fused_linear_cross_entropy(flat, w_out, labels.reshape(-1), ignore_index=ignore_index), None
+            # the kernels read the bf16 copy; dW lands in the fp32 (tied) weight unrounded
+            return fused_linear_cross_entropy(flat, self.output.weight, labels.reshape(-1), ignore_index=ignore_index,
+                                              compute_weight=pw_out.value()), None
+        w_out = pw_out.get()
         logits = F.linear(normed, w_out).float()
         loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]), labels.reshape(-1), ignore_index=ignore_index)
         return loss, logits

@@ -152,6 +152,13 @@ class PackedWeights:
             return _PackedGrad.apply(self, self.tensor, *self.params)
         return self.tensor
 
+    def value(self) -> torch.Tensor:
+        """The current packed bf16 weights outside the autograd graph (for an operator
+        that sends its weight gradient to the fp32 parameter itself)."""
+        if self._stale():
+            self.refresh()
+        return self.tensor
+
 
 class AdamWShadow(torch.optim.Optimizer):
     """``torch.optim.AdamW`` (decoupled weight decay) on fp32 CUDA parameters in one

@@ -22,7 +22,7 @@ def test_header_declares_the_hot_path():
     names = _declared()
     for n in ("mt_rms_norm_fwd", "mt_rms_norm_bwd", "mt_add_rms_norm_fwd", "mt_add_rms_norm_bwd", "mt_rope",
               "mt_swiglu_fwd", "mt_swiglu_bwd", "mt_attention_fwd", "mt_attention_bwd", "mt_fused_ce_fwd",
-              "mt_fused_ce_grad_logits"):
+              "mt_fused_ce_bwd", "mt_debug_wait_timeout"):
         assert n in names
 
 

@@ -121,9 +121,19 @@ def _ce_config2(dev, ignore_every, weight_dtype):
     hd = hidden.detach().requires_grad_(True)
     wd = weight.detach().requires_grad_(True)
     loss = K.triton_fused_linear_cross_entropy(hd, wd, labels, ignore_index=-100)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
     (loss * 0.5).backward()
     torch.cuda.synchronize()
     assert _lib.read_status(dev) == 0
+    # the backward never holds an [N, V] logit gradient (2.8 GB here): only dH, dW and
+    # the workspace (row inputs, fp32 split partials) are allocated
+    grads = hd.grad.numel() * hd.grad.element_size() + wd.grad.numel() * wd.grad.element_size()
+    ws = int(_lib.load().mt_fused_ce_bwd_workspace_bytes(N2, V, H))
+    delta = torch.cuda.max_memory_allocated(dev) - base
+    assert delta <= grads + ws + (64 << 20), (delta, grads, ws)
+    assert delta < N2 * V * 2 // 2, delta
     assert wd.grad.dtype == weight_dtype
     # oracle on the bf16-rounded operands, as the kernels see them
     lo, dho, dwo = O.linear_cross_entropy_grads(hidden.float(), weight.to(torch.bfloat16).float(), labels, -100,

@@ -75,6 +75,65 @@ def test_fused_ce_shapes(cuda_device, rows, hdim, vocab, seed, ignore_every, int
     _check_grads(dh, dho, dw, dwo)
 
 
+@pytest.mark.parametrize("rows,hdim,vocab,seed", [
+    (1000, 1024, 3000, 11),   # hidden split over a cluster of 3 CTAs (384 + 384 + 256)
+    (200, 1280, 500, 12),     # two hidden-column groups (1152 + 128)
+    (64, 104, 300, 13),       # one partial 128-column slice
+    (4096, 256, 21504, 14),   # BASELINE config-0 widths: one CTA per cluster, vocab split
+    (130, 768, 129, 15),      # ragged rows and vocab tiles
+])
+def test_fused_ce_backward_shapes(cuda_device, rows, hdim, vocab, seed):
+    loss, lo, dh, dho, dw, dwo = _case(cuda_device, rows, hdim, vocab, seed, ignore_every=9, grad_scale=1.3)
+    rel = abs(float(loss.detach()) - float(lo.detach())) / abs(float(lo.detach()))
+    assert rel <= 1e-3, f"loss rel err {rel:.3e}"
+    _check_grads(dh, dho, dw, dwo)
+
+
+def test_fused_ce_fp32_master_weight(cuda_device):
+    """fp32 weight (the reference's autocast case): the kernels read its bf16 rounding and dW
+    comes back in fp32, accumulated without a 16-bit rounding (triton_ops.py:352-357)."""
+    from mega_trading_b200.kernels import fused_ce as F
+    from mega_trading_b200.kernels import triton_ops as K
+
+    g = torch.Generator().manual_seed(21)
+    hidden = (torch.randn(512, 768, generator=g) * 0.5).to(torch.bfloat16)
+    weight = torch.randn(5000, 768, generator=g) * 0.02
+    labels = torch.randint(0, 5000, (512,), generator=g)
+    hd = hidden.to(cuda_device).requires_grad_(True)
+    wd = weight.to(cuda_device).requires_grad_(True)
+    loss = K.triton_fused_linear_cross_entropy(hd, wd, labels.to(cuda_device))
+    loss.backward()
+    assert wd.grad.dtype == torch.float32 and hd.grad.dtype == torch.bfloat16
+    ho = hidden.float().requires_grad_(True)
+    wo = weight.to(torch.bfloat16).float().requires_grad_(True)
+    O.linear_cross_entropy(ho, wo, labels, -100).backward()
+    _check_grads(hd.grad, ho.grad, wd.grad, wo.grad)
+    # the fp32 gradient is not a 16-bit value: it carries bits below bf16's mantissa
+    assert bool((wd.grad != wd.grad.to(torch.bfloat16).float()).any())
+    # a 16-bit compute copy with the gradient sent to the fp32 weight (the model's path)
+    wd2 = weight.to(cuda_device).requires_grad_(True)
+    hd2 = hidden.to(cuda_device).requires_grad_(True)
+    loss2 = F.fused_linear_cross_entropy(hd2, wd2, labels.to(cuda_device), compute_weight=wd2.detach().bfloat16())
+    loss2.backward()
+    assert torch.equal(loss2, loss.detach())
+    assert torch.equal(wd2.grad, wd.grad) and torch.equal(hd2.grad, hd.grad)
+
+
+def test_fused_ce_backward_is_deterministic(cuda_device):
+    from mega_trading_b200.kernels import triton_ops as K
+
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    h = torch.randn(3000, 768, device=cuda_device, generator=g).bfloat16()
+    w = (torch.randn(21504, 768, device=cuda_device, generator=g) * 0.02).bfloat16()
+    lab = torch.randint(0, 21504, (3000,), device=cuda_device, generator=g)
+    grads = []
+    for _ in range(2):
+        hd, wd = h.clone().requires_grad_(True), w.float().requires_grad_(True)
+        K.triton_fused_linear_cross_entropy(hd, wd, lab).backward()
+        grads.append((hd.grad, wd.grad))
+    assert torch.equal(grads[0][0], grads[1][0]) and torch.equal(grads[0][1], grads[1][1])
+
+
 def test_fused_ce_all_ignored(cuda_device):
     from mega_trading_b200.kernels import triton_ops as K
 
