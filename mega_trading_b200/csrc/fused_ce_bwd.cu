@@ -31,9 +31,10 @@
 // by CTA c: a [128 x 128] 16-bit tile in the K-major 128B-swizzled layout the
 // MMA's A operand reads) and a ring of 32 KB stages fed by TMA: for a logit
 // tile, per 64-column K chunk, the fixed-side box and the stream-side box
-// (K-major operands of S); for the output product, two 64-column panels of
-// the stream tile's slice, which the MMA reads MN-major (the same bytes, the
-// other operand role).  Warp roles (320 threads): warps 0-7 epilogue (thread =
+// (K-major operands of S); for the output product, 128 output columns x the
+// tile's 128 stream entities of a transposed copy of the stream operand (made
+// by a transpose kernel in the workspace), so that both products read K-major
+// operands (an MN-major B measured ~2x slower per instruction).  Warp roles (320 threads): warps 0-7 epilogue (thread =
 // TMEM lane = fixed-side entity; warpgroup w takes logit columns [64w, 64w+64)
 // and output panels p = w mod 2), warp 8 TMA producer + TMEM allocation,
 // warp 9 MMA issuer.
@@ -79,6 +80,7 @@ struct BwdCfg {
 struct BwdParams {
   CUtensorMap tm_f;  // fixed-side operand [f_count, K] (H for MODE 0, W for MODE 1), box 64 x 128
   CUtensorMap tm_x;  // stream-side operand [x_count, K], box 64 x 128
+  CUtensorMap tm_xt; // its transpose [K, x_pad] (x_pad = x_count rounded to 8), box 64 x 128
   const float4* rinfo;  // per row: {-lse2, g, label bits, 0}; rows padded to a multiple of 128 with zeros
   int n_kc;             // 64-column chunks of K
   int f_count;          // entities of the fixed side
@@ -86,6 +88,7 @@ struct BwdParams {
   int n_x_tiles;        // stream tiles in total
   int x_tiles_per_split;
   int slice_w;          // output columns per CTA (multiple of 64, <= 384)
+  int stagger_mod, stagger_step;  // stream start of fixed tile y: (y % mod) * step tiles
   int hid0;             // first output column of this launch
   int hid_end;          // one past the last output column of this launch
   void* out;            // [f_count, out_ld] (+ split * split_stride): dH / dW or fp32 partials
@@ -202,8 +205,15 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
   const int hid_base = p.hid0 + s * p.slice_w;
   const int n_panels = p.slice_w / kKC;
   const int n_ostages = (n_panels + 1) / 2;
-  auto tile_of = [&](int t, int c) { return xs0 + t * C + c; };
-  auto exists = [&](int t, int c) { return t < n_rounds && tile_of(t, c) < xs1; };
+  // clusters start their stream at staggered tiles (same order, rotated), so
+  // the clusters resident at one time do not all read the same tile at once
+  const int rot = n_x > 0 ? (int)(((int64_t)(blockIdx.y % p.stagger_mod) * p.stagger_step) % n_x) : 0;
+  auto tile_of = [&](int t, int c) {
+    int i = t * C + c + rot;
+    if (i >= n_x) i -= n_x;
+    return xs0 + i;
+  };
+  auto exists = [&](int t, int c) { return t < n_rounds && t * C + c < n_x; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::NST; ++i) {
@@ -245,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_f);
       tma_prefetch_desc(&p.tm_x);
+      tma_prefetch_desc(&p.tm_xt);
       int it = 0;
       bool ok = true;
       auto next_stage = [&](uint32_t bytes) -> uint8_t* {
@@ -265,13 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
           ++it;
         }
       };
+      // the output product's B operand: 128 output columns x the tile's 128
+      // stream entities, K-major from the transposed operand (two 64-entity atoms)
       auto load_panels = [&](int xt) {
         for (int q = 0; ok && q < n_ostages; ++q) {
-          const int np = min(2, n_panels - 2 * q);
-          uint8_t* sa = next_stage(np * kBox);
+          uint8_t* sa = next_stage(kStage);
           if (!ok) break;
-          for (int e = 0; e < np; ++e)
-            tma_load_2d(sa + e * kBox, &p.tm_x, &full[it % Cfg::NST], hid_base + (2 * q + e) * kKC, xt * kT);
+          for (int e = 0; e < 2; ++e)
+            tma_load_2d(sa + e * kBox, &p.tm_xt, &full[it % Cfg::NST], xt * kT + e * kKC, hid_base + q * 128);
           ++it;
         }
       };
@@ -314,10 +326,12 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
           }
           tc_fence_after();
           const uint32_t a = stage_base + st * kStage;
+          // a K step of 16 elements advances the start address by 32 bytes (2 in the descriptor)
+          const uint64_t da = make_sdesc(a, 16, 1024, kSwizzle128);
+          const uint64_t db = make_sdesc(a + kBox, 16, 1024, kSwizzle128);
 #pragma unroll
           for (int kk = 0; kk < kKC / 16; ++kk)
-            umma_ss(tmem + kSCol, make_sdesc(a + kk * 32, 16, 1024, kSwizzle128),
-                    make_sdesc(a + kBox + kk * 32, 16, 1024, kSwizzle128), idesc_s, (kc > 0 || kk > 0) ? 1u : 0u);
+            umma_ss(tmem + kSCol, da + 2 * kk, db + 2 * kk, idesc_s, (kc > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[st]);
         }
         umma_commit(s_full);
@@ -343,12 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
           }
           tc_fence_after();
           const int np = min(2, n_panels - 2 * q);
-          const uint32_t idesc_o = make_idesc(kT, np * kKC, kBf16, 0, 1);
+          const uint32_t idesc_o = make_idesc(kT, np * kKC, kBf16, 0, 0);
           const uint32_t b0 = stage_base + st * kStage;
+          const uint64_t da[2] = {make_sdesc(a0, 16, 1024, kSwizzle128), make_sdesc(a0 + kBox, 16, 1024, kSwizzle128)};
+          const uint64_t db[2] = {make_sdesc(b0, 16, 1024, kSwizzle128), make_sdesc(b0 + kBox, 16, 1024, kSwizzle128)};
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
-            umma_ss(tmem + q * 128, make_sdesc(a0 + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024, kSwizzle128),
-                    make_sdesc(b0 + kk * 2048, kBox, 1024, kSwizzle128), idesc_o,
+            umma_ss(tmem + q * 128, da[kk >> 2] + 2 * (kk & 3), db[kk >> 2] + 2 * (kk & 3), idesc_o,
                     (first_out && kk == 0) ? 0u : 1u);
           umma_commit(&empty[st]);
         }
@@ -387,6 +402,13 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
     const int r = threadIdx.x & 127;  // TMEM lane = fixed-side entity of the tile
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     float4* ri_s = reinterpret_cast<float4*>(smem + Cfg::OFF_RINFO);
+    // One thread polls a barrier while the other epilogue warps sleep in a
+    // named barrier (polling warps would take issue slots from the MMA warp
+    // on the same sub-partition); the poller's verdict reaches all 256.
+    auto epi_wait = [&](auto&& wait_fn) -> bool {
+      const bool v = threadIdx.x == 0 ? wait_fn() : true;
+      return bar_all(v, 3, 256);
+    };
     const int fe = f0 + r;  // this thread's fixed-side entity
     // MODE 0: the thread's row; MODE 1: the thread's vocab entry
     float nlse2 = 0.f, g = 0.f;
@@ -406,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
     for (int t = 0; t < n_rounds; ++t) {
       if (!exists(t, s)) break;
       const int xt = tile_of(t, s);
-      if (!__all_sync(0xffffffffu, wait_bounded(wc, s_full, n_own & 1, 8))) {
+      if (!epi_wait([&] { return wait_bounded(wc, s_full, n_own & 1, 8); })) {
         ok = false;
         break;
       }
@@ -432,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
         dz_cols_vocab<T>(z1, ri_s + wg * 64 + 32, fe, fe_ok, pk1);
       }
       // the slot's previous tile must be consumed by every CTA of the cluster
-      if (n_own > 0 && !__all_sync(0xffffffffu, wait_x(&dz_free[s], (n_own - 1) & 1, 9))) {
+      if (n_own > 0 && !epi_wait([&] { return wait_x(&dz_free[s], (n_own - 1) & 1, 9); })) {
         ok = false;
         break;
       }
@@ -461,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1) ce_bwd_kernel(const __grid_consta
     }
     // every CTA has finished with this CTA's last dZ tile: no copy or commit
     // addressed to this CTA is still in flight when it exits
-    if (n_own > 0) wait_drain(wc, &dz_free[s], (n_own - 1) & 1, 10);
+    if (n_own > 0 && threadIdx.x == 0) wait_drain(wc, &dz_free[s], (n_own - 1) & 1, 10);
     if (ok && !*abort_flag && n_x > 0) {
-      if (__all_sync(0xffffffffu, wait_bounded(wc, acc_full, 0, 6))) {
+      if (epi_wait([&] { return wait_bounded(wc, acc_full, 0, 6); })) {
         tc_fence_after();
         const bool store = fe < p.f_count && fe_ok;
         char* out_row = static_cast<char*>(p.out) +
@@ -585,7 +607,7 @@ int choose_splits(int64_t fixed_tiles, int64_t stream_tiles, int C, double flops
 struct BwdPlan {
   int64_t Np;
   int splits[2];  // MODE 0 (dH), MODE 1 (dW)
-  int64_t rinfo_bytes, part_bytes, bytes;
+  int64_t rinfo_bytes, part_bytes, xt_bytes, bytes;
 };
 
 BwdPlan plan_bwd(int64_t N, int64_t V, int64_t K) {
@@ -602,8 +624,28 @@ BwdPlan plan_bwd(int64_t N, int64_t V, int64_t K) {
   const int64_t p0 = pl.splits[0] > 1 ? int64_t(pl.splits[0]) * pl.Np * K * 4 : 0;
   const int64_t p1 = pl.splits[1] > 1 ? int64_t(pl.splits[1]) * voc_tiles * kT * K * 4 : 0;
   pl.part_bytes = up(std::max(p0, p1));
-  pl.bytes = pl.rinfo_bytes + pl.part_bytes + 256;
+  // transposed stream operand of either pass (one at a time): [K, entities rounded to 128]
+  pl.xt_bytes = up(K * std::max(pl.Np, voc_tiles * kT) * 2);
+  pl.bytes = pl.rinfo_bytes + pl.part_bytes + pl.xt_bytes + 256;
   return pl;
+}
+
+// out[k, r] = in[r, k] for r < rows, 0 for rows <= r < ld_out (64 x 64 tiles through shared memory).
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ in, int64_t rows, int64_t K,
+                                                        T* __restrict__ out, int64_t ld_out) {
+  __shared__ T tile[64][66];
+  const int64_t r0 = int64_t(blockIdx.x) * 64, k0 = int64_t(blockIdx.y) * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4 threads
+  for (int i = ty; i < 64; i += 4) {
+    const int64_t r = r0 + i, k = k0 + tx;
+    tile[i][tx] = (r < rows && k < K) ? in[r * K + k] : from_f32<T>(0.f);
+  }
+  __syncthreads();
+  for (int i = ty; i < 64; i += 4) {
+    const int64_t k = k0 + i, r = r0 + tx;
+    if (k < K && r < ld_out) out[k * ld_out + r] = tile[tx][i];
+  }
 }
 
 int map_rows(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t K) {
@@ -669,13 +711,22 @@ int reduce_splits(const float* part, int splits, int64_t split_stride, int64_t r
 
 // One pass (MODE 0: dH, MODE 1: dW) over every slice group of the hidden columns.
 template <typename T, int MODE>
-int run_pass(const BwdPlan& pl, const void* fixed, int64_t f_count, const void* stream_op, int64_t x_count,
+int run_pass(const BwdPlan& pl, const void* fixed, int64_t f_count, const void* stream_op, int64_t x_count, void* xt,
              int dtype, int64_t V, int64_t K, const float4* rinfo, float* part, void* out, int out_dtype,
              uint32_t* status, cudaStream_t s) {
   BwdParams prm;
   int st = map_rows(&prm.tm_f, dtype, fixed, f_count, K);
   if (st != MT_OK) return st;
   if ((st = map_rows(&prm.tm_x, dtype, stream_op, x_count, K)) != MT_OK) return st;
+  // the output products read the stream operand K-major: a transposed copy
+  const int64_t x_pad = (x_count + kT - 1) / kT * kT;
+  {
+    dim3 grid((unsigned)(x_pad / 64), (unsigned)((K + 63) / 64));
+    transpose_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(stream_op), x_count, K, static_cast<T*>(xt),
+                                              x_pad);
+    if ((st = check_launch("fused_ce_bwd_transpose")) != MT_OK) return st;
+    if ((st = map_rows(&prm.tm_xt, dtype, xt, K, x_pad)) != MT_OK) return st;
+  }
   const int64_t fixed_tiles = (f_count + kT - 1) / kT;
   const int64_t x_tiles = (x_count + kT - 1) / kT;
   const int64_t per_split = (x_tiles + pl.splits[MODE] - 1) / pl.splits[MODE];
@@ -687,6 +738,11 @@ int run_pass(const BwdPlan& pl, const void* fixed, int64_t f_count, const void* 
   prm.V = (int)V;
   prm.n_x_tiles = (int)x_tiles;
   prm.x_tiles_per_split = (int)per_split;
+  // MODE 0 streams the (L2-resident) weight: starts spread over all of it;
+  // MODE 1 streams the hidden states, which may not fit in L2: starts within
+  // a window of 16 tiles, so their reads still meet in L2
+  prm.stagger_mod = 16;
+  prm.stagger_step = MODE == 0 ? (int)std::max<int64_t>(1, per_split / 16) : 1;
   prm.status = status;
   const int64_t f_pad = fixed_tiles * kT;
   if (splits > 1) {
@@ -761,19 +817,20 @@ extern "C" int mt_fused_ce_bwd(const void* hidden, const void* weight, const voi
   char* ws = static_cast<char*>(workspace);
   float4* rinfo = reinterpret_cast<float4*>(ws);
   float* part = reinterpret_cast<float*>(ws + pl.rinfo_bytes);
+  void* xt = ws + pl.rinfo_bytes + pl.part_bytes;
   ce_rowinfo_kernel<<<(unsigned)((pl.Np + 255) / 256), 256, 0, s>>>(labels, labels_i64, ignore_index, (int)N,
                                                                     (int)pl.Np, (int)V, lse2_scal, lse2_scal + N,
                                                                     grad_out, rinfo);
   if ((st = check_launch("fused_ce_bwd_rowinfo")) != MT_OK) return st;
   const bool bf = dtype == MT_BF16;
   if (dhidden != nullptr) {
-    st = bf ? run_pass<__nv_bfloat16, 0>(pl, hidden, N, weight, V, dtype, V, K, rinfo, part, dhidden, dh_dtype, status, s)
-            : run_pass<__half, 0>(pl, hidden, N, weight, V, dtype, V, K, rinfo, part, dhidden, dh_dtype, status, s);
+    st = bf ? run_pass<__nv_bfloat16, 0>(pl, hidden, N, weight, V, xt, dtype, V, K, rinfo, part, dhidden, dh_dtype, status, s)
+            : run_pass<__half, 0>(pl, hidden, N, weight, V, xt, dtype, V, K, rinfo, part, dhidden, dh_dtype, status, s);
     if (st != MT_OK) return st;
   }
   if (dweight != nullptr) {
-    st = bf ? run_pass<__nv_bfloat16, 1>(pl, weight, V, hidden, N, dtype, V, K, rinfo, part, dweight, dw_dtype, status, s)
-            : run_pass<__half, 1>(pl, weight, V, hidden, N, dtype, V, K, rinfo, part, dweight, dw_dtype, status, s);
+    st = bf ? run_pass<__nv_bfloat16, 1>(pl, weight, V, hidden, N, xt, dtype, V, K, rinfo, part, dweight, dw_dtype, status, s)
+            : run_pass<__half, 1>(pl, weight, V, hidden, N, xt, dtype, V, K, rinfo, part, dweight, dw_dtype, status, s);
     if (st != MT_OK) return st;
   }
   return MT_OK;

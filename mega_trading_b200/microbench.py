@@ -330,6 +330,112 @@ def qkv_cases(dev, iters, profile, n=65536, h=768, hq=12, hkv=4, d=64, seq=2048)
              "unfused_ms": mu}]
 
 
+REF_DIR = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+
+
+def load_reference(ref_dir: Path = REF_DIR):
+    """Import duoan/mega-trading's own operator modules from an installed copy
+    (``pip install --target baseline/_ref``) through a stub package: the real
+    ``mega_trading/__init__.py`` imports the trainer, which needs ``accelerate``.
+    Returns ``(triton_attention module, triton_ops module, model module)`` or None."""
+    import sys
+    import types
+
+    src = ref_dir / "mega_trading"
+    if not (src / "kernels" / "triton_ops.py").exists():
+        return None
+    if "mega_trading" not in sys.modules:
+        pkg = types.ModuleType("mega_trading")
+        pkg.__path__ = [str(src)]
+        sys.modules["mega_trading"] = pkg
+    import importlib
+
+    return (importlib.import_module("mega_trading.kernels.triton_attention"),
+            importlib.import_module("mega_trading.kernels.triton_ops"),
+            importlib.import_module("mega_trading.model"))
+
+
+def reference_cases(dev, iters, seqs=(1024, 2048, 4096), n=65536):
+    """The reference's own GPU kernels (Triton, JIT-compiled for this GPU) on the same inputs and
+    harness as ours: config-1 attention forward / backward, config-2 RMSNorm, add+RMSNorm, RoPE,
+    SwiGLU gate and fused linear + CE.  Where the reference falls back to torch (its backward
+    outside T=512 materialises fp32 T x T tensors) that is what gets timed; an out-of-memory is
+    recorded as such."""
+    ref = load_reference()
+    if ref is None:
+        return [{"op": "reference", "unavailable": f"no installed reference under {REF_DIR}"}]
+    RA, RO, _ = ref
+    out = []
+
+    def timed(name, fn, **meta):
+        try:
+            ms = _time(fn, iters)
+            out.append({"op": name, "ms": ms, **meta})
+            return ms
+        except torch.OutOfMemoryError as exc:
+            out.append({"op": name, "oom": str(exc).splitlines()[0][:160], **meta})
+            torch.cuda.empty_cache()
+            return None
+
+    for T in seqs:
+        B, Hq, Hkv, D = 16, 16, 4, 64
+        g = torch.Generator(device=dev).manual_seed(T)
+        q = (torch.randn(B, Hq, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        k = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        v = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+        do = torch.randn(B, Hq, T, D, device=dev, generator=g).bfloat16()
+        flops = 4.0 * B * Hq * D * T * (T + 1) / 2
+        mf = timed("ref_attention_fwd", lambda: RA.triton_attention(q, k, v, repeats=Hq // Hkv), T=T)
+        if mf:
+            out[-1]["tflops"] = flops / mf / 1e9
+        try:
+            o = RA.triton_attention(q, k, v, repeats=Hq // Hkv)
+            mb = timed("ref_attention_bwd", lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True), T=T)
+            if mb:
+                out[-1]["tflops"] = 2.5 * flops / mb / 1e9
+            del o
+        except torch.OutOfMemoryError as exc:
+            out.append({"op": "ref_attention_bwd", "T": T, "oom": str(exc).splitlines()[0][:160]})
+        del q, k, v, do
+        torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(9)
+    H, I, V = 768, 2048, 21504
+    bf = torch.bfloat16
+    x = torch.randn(n, H, device=dev, generator=g).to(bf)
+    r = torch.randn(n, H, device=dev, generator=g).to(bf)
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).to(bf)
+    ms = timed("ref_rms_norm_fwd", lambda: RO.triton_rms_norm(x, w, eps=1e-5), N=n)
+    if ms:
+        out[-1]["gbs"] = (2 * n * H * 2 + 4 * n) / ms / 1e6
+    ms = timed("ref_add_rms_norm_fwd", lambda: RO.triton_add_rms_norm(x, r, w, eps=1e-5), N=n)
+    if ms:
+        out[-1]["gbs"] = 4 * n * H * 2 / ms / 1e6
+    del x, r
+    gt = torch.randn(n, I, device=dev, generator=g).to(bf)
+    up = torch.randn(n, I, device=dev, generator=g).to(bf)
+    ms = timed("ref_swiglu_fwd", lambda: RO.triton_swiglu_gate(gt, up), N=n)
+    if ms:
+        out[-1]["gbs"] = 3 * n * I * 2 / ms / 1e6
+    del gt, up
+    Bt, T, D = n // 2048, 2048, 64
+    qr = torch.randn(Bt, 12, T, D, device=dev, generator=g).to(bf)
+    kr = torch.randn(Bt, 4, T, D, device=dev, generator=g).to(bf)
+    fr = torch.outer(torch.arange(T, device=dev, dtype=torch.float32),
+                     1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)))
+    c, sn = fr.cos().to(bf)[None, None], fr.sin().to(bf)[None, None]
+    ms = timed("ref_rope", lambda: RO.triton_apply_rope(qr, kr, c, sn), N=n)
+    if ms:
+        out[-1]["gbs"] = 2 * n * 16 * D * 2 / ms / 1e6
+    del qr, kr
+    hid = (torch.randn(n, H, device=dev, generator=g) * 0.5).to(bf).requires_grad_(True)
+    wv = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(bf).requires_grad_(True)
+    lab = torch.randint(0, V, (n,), device=dev, generator=g)
+    ms = timed("ref_fused_ce_fwd_bwd", lambda: RO.triton_fused_linear_cross_entropy(hid, wv, lab).backward(), N=n)
+    if ms:
+        out[-1]["tflops"] = 6.0 * n * H * V / ms / 1e9
+    return out
+
+
 def torch_comparators(dev, iters, seqs=(1024, 2048, 4096), n=65536):
     """The BASELINE torch comparators on the same box: SDPA (flash / cuDNN backends) for causal
     GQA attention at config 1, F.rms_norm, eager RoPE, F.silu * up and F.linear + F.cross_entropy
@@ -402,6 +508,8 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += qkv_cases(dev, iters, profile, n=ce_rows)
     if "torch" in ops and not profile:
         res += torch_comparators(dev, iters, attn_seqs)
+    if "ref" in ops and not profile:
+        res += reference_cases(dev, iters, attn_seqs)
     bw = [o for o in ops if o in ("rmsnorm", "addrmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))
