@@ -247,6 +247,28 @@ def bandwidth_cases(dev, iters, profile, ops=("rmsnorm", "addrmsnorm", "rope", "
     return out
 
 
+def adamw_cases(dev, iters, profile, model: str = "gqa12"):
+    """The fused AdamW over every parameter of a BASELINE model (config 3: 92 M fp32 parameters),
+    writing the bf16 GEMM-operand copies; 30 bytes per parameter (p, g, m, v read; p, m, v
+    written; 2-byte copy)."""
+    from .model import CONFIGS, TradingModelB200
+    from .optim import AdamWShadow
+
+    torch.manual_seed(0)
+    m = TradingModelB200(CONFIGS[model]).to(dev)
+    opt = AdamWShadow(m.parameters(), lr=1e-4, weight_decay=0.01, packed=m.packed_weights())
+    for p in m.parameters():
+        p.grad = torch.randn_like(p) * 1e-3
+    numel = sum(p.numel() for p in m.parameters())
+    step = lambda: opt.step()  # noqa: E731
+    if profile:
+        for _ in range(iters):
+            step()
+        return []
+    ms = _time(step, iters)
+    return [{"op": "adamw", "model": model, "params": numel, "ms": ms, "gbs": 30.0 * numel / ms / 1e6}]
+
+
 def mlp_cases(dev, iters, profile, n=65536, h=768, inter=2048):
     """SwiGLU MLP: the fused tcgen05 GEMMs against cuBLAS + the standalone packed gate."""
     import torch.nn.functional as F
@@ -510,6 +532,8 @@ def run(ops: list[str], iters: int = 10, profile: bool = False, device: int = 0,
         res += torch_comparators(dev, iters, attn_seqs)
     if "ref" in ops and not profile:
         res += reference_cases(dev, iters, attn_seqs)
+    if "adamw" in ops:
+        res += adamw_cases(dev, iters, profile)
     bw = [o for o in ops if o in ("rmsnorm", "addrmsnorm", "rope", "swiglu")]
     if bw:
         res += bandwidth_cases(dev, iters, profile, tuple(bw))
