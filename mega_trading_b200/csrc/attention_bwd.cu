@@ -324,18 +324,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
       const uint32_t ds_base = smem_u32(sDS);
+      // Descriptors are built once per operand tile and stepped by adding to
+      // the start-address field (bytes / 16), which keeps the issue loop short:
+      // the next MMA goes out only when this thread reaches it, and per-MMA
+      // descriptor arithmetic measured ~12 cycles per N = 64 instruction.
+      const uint64_t dk0 = make_sdesc(k_base, 16, C::SBO, C::LAYOUT);
+      const uint64_t dv0 = make_sdesc(v_base, 16, C::SBO, C::LAYOUT);
+      const uint64_t dk_mn0 = make_sdesc(k_base, C::TILE, C::SBO, C::LAYOUT);
+      const uint64_t ds_k0 = make_sdesc(ds_base, 16, 1024, kSwizzle128);
+      const uint64_t ds_mn0 = make_sdesc(ds_base, 128 * 128, 1024, kSwizzle128);
+      constexpr uint32_t kRowStep = 16 * C::ROW_BYTES / 16;  // 16 rows of a tile, in descriptor units
       auto issue_sdp = [&](int st) {
         const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
+        const uint64_t dq = make_sdesc(qb, 16, C::SBO, C::LAYOUT), ddo = make_sdesc(dob, 16, C::SBO, C::LAYOUT);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          umma_ss(tmem + C::T_S, make_sdesc(k_base + kk * 32, 16, C::SBO, C::LAYOUT),
-                  make_sdesc(qb + kk * 32, 16, C::SBO, C::LAYOUT), idesc_sd, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + C::T_S, dk0 + 2 * kk, dq + 2 * kk, idesc_sd, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          umma_ss(tmem + C::T_DP, make_sdesc(v_base + kk * 32, 16, C::SBO, C::LAYOUT),
-                  make_sdesc(dob + kk * 32, 16, C::SBO, C::LAYOUT), idesc_sd, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + C::T_DP, dv0 + 2 * kk, ddo + 2 * kk, idesc_sd, kk > 0 ? 1u : 0u);
         umma_commit(bar_sd_full);
       };
       // Issue order per tile i: S/dP of tile i+1 as soon as the compute warps
@@ -376,22 +383,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           }
           tc_fence_after();
           const uint32_t qb = q_base + st * C::TILE, dob = do_base + st * C::TILE;
+          const uint64_t ddo_mn = make_sdesc(dob, C::TILE, C::SBO, C::LAYOUT);
+          const uint64_t dq_mn = make_sdesc(qb, C::TILE, C::SBO, C::LAYOUT);
           // dV += P^T dO ; dK += dS^T Q   (K = 128 queries in steps of 16)
 #pragma unroll
           for (int kk = 0; kk < kBQ / 16; ++kk) {
-            const uint32_t b_off = kk * 16 * C::ROW_BYTES;
             const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-            umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, make_sdesc(dob + b_off, C::TILE, C::SBO, C::LAYOUT),
-                    idesc_acc, acc);
+            umma_ts(tmem + C::T_DV, tmem + C::T_PT + kk * 8, ddo_mn + kRowStep * kk, idesc_acc, acc);
           }
           umma_commit(bar_pt_free);
 #pragma unroll
           for (int kk = 0; kk < kBQ / 16; ++kk) {
-            const uint32_t a_off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-            const uint32_t b_off = kk * 16 * C::ROW_BYTES;
+            // dS^T K-major: 64-column atoms of 128 x 128 bytes, 32 bytes per K step inside an atom
+            const uint32_t a_step = (kk >> 2) * (128 * 128 / 16) + (kk & 3) * 2;
             const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-            umma_ss(tmem + C::T_DK, make_sdesc(ds_base + a_off, 16, 1024, kSwizzle128),
-                    make_sdesc(qb + b_off, C::TILE, C::SBO, C::LAYOUT), idesc_acc, acc);
+            umma_ss(tmem + C::T_DK, ds_k0 + a_step, dq_mn + kRowStep * kk, idesc_acc, acc);
           }
           umma_commit(&bar_q_empty[st]);  // Q/dO of this stage are no longer read (dQ reads K and dS)
           if (ci > 0 && !wait_bounded(wc, bar_dq_free, (ci - 1) & 1, 6)) {
@@ -401,11 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kernel(const __grid_cons
           tc_fence_after();
           // dQ = dS K   (M = 128 queries, K = 128 keys in steps of 16)
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_ss(tmem + C::T_DQ, make_sdesc(ds_base + kk * 2048, 128 * 128, 1024, kSwizzle128),
-                    make_sdesc(k_base + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT), idesc_dq,
-                    kk > 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_ss(tmem + C::T_DQ, ds_mn0 + (2048 / 16) * kk, dk_mn0 + kRowStep * kk, idesc_dq, kk > 0 ? 1u : 0u);
           umma_commit(bar_dq_full);
           if (j + 1 == w.n_it) umma_commit(bar_item);
         }

@@ -254,22 +254,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t k_base = smem_u32(sK);
       const uint32_t v_base = smem_u32(sV);
+      // Descriptors built once per tile and stepped in the start-address field
+      // (bytes / 16): the next MMA goes out only when this thread reaches it,
+      // so the issue loop carries no per-MMA descriptor arithmetic.
       auto issue_s = [&](int slot, int st) {
+        const uint64_t ad = make_sdesc(q_base + slot * C::TILE, 16, C::SBO, C::LAYOUT);
+        const uint64_t bd = make_sdesc(k_base + st * C::TILE, 16, C::SBO, C::LAYOUT);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t ad = make_sdesc(q_base + slot * C::TILE + kk * 32, 16, C::SBO, C::LAYOUT);
-          const uint64_t bd = make_sdesc(k_base + st * C::TILE + kk * 32, 16, C::SBO, C::LAYOUT);
-          umma_ss(tmem + slot * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < D / 16; ++kk) umma_ss(tmem + slot * 256, ad + 2 * kk, bd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
       };
       auto issue_pv = [&](int slot, int st, bool acc_first) {
         // A = P from TMEM (16 keys = 8 packed columns per step), B = V (MN-major)
+        const uint64_t bd = make_sdesc(v_base + st * C::TILE, C::TILE, C::SBO, C::LAYOUT);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = make_sdesc(v_base + st * C::TILE + kk * 16 * C::ROW_BYTES, C::TILE, C::SBO, C::LAYOUT);
-          umma_ts(tmem + slot * 256 + C::T_O, tmem + slot * 256 + C::T_P + kk * 8, bd, idesc_o,
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_ts(tmem + slot * 256 + C::T_O, tmem + slot * 256 + C::T_P + kk * 8, bd + kk * C::ROW_BYTES, idesc_o,
                   (acc_first || kk > 0) ? 1u : 0u);
-        }
       };
       // One issuing thread per slot: each slot's S(j+1) goes out as soon as
       // that slot has read S(j), and its P V(j) as soon as it has written
