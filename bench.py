@@ -212,6 +212,16 @@ def main(argv: list[str] | None = None) -> int:
                     help="gqa12 = BASELINE config 3 (default), large24 = config 4")
     ap.add_argument("--micro-batch", type=int, default=None, help="sequences per micro-step and rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="analysis only: override the workload's global batch (the metric then no longer matches "
+                         "the BASELINE configuration)")
+    ap.add_argument("--bucket-mb", type=int, default=64, help="DDP gradient bucket size (MB)")
+    ap.add_argument("--comm-priority", choices=("high", "normal"), default="high",
+                    help="stream priority of the gradient all-reduce")
+    ap.add_argument("--comm-max-ctas", type=int, default=None, help="cap on the CTAs NCCL uses per collective")
+    ap.add_argument("--phase-split", action="store_true",
+                    help="also time the phases of each step (forward, backward, the last backward with the "
+                         "gradient all-reduce, optimizer) with CUDA events on every rank")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
@@ -224,7 +234,11 @@ def main(argv: list[str] | None = None) -> int:
 
     wl = WORKLOADS[args.model]
     METRIC, GLOBAL_BATCH, SEQ = wl["metric"], wl["global_batch"], wl["seq"]
-    rank, world, local = init_distributed("nccl")
+    if args.global_batch:
+        GLOBAL_BATCH = int(args.global_batch)
+        METRIC += f" [analysis run: global batch {GLOBAL_BATCH}]"
+    rank, world, local = init_distributed("nccl", comm_high_priority=args.comm_priority == "high",
+                                          comm_max_ctas=args.comm_max_ctas)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if GLOBAL_BATCH % world:
@@ -232,7 +246,7 @@ def main(argv: list[str] | None = None) -> int:
     cfg = CONFIGS[args.model]
     local_batch = GLOBAL_BATCH // world
     micro = min(args.micro_batch or wl["micro_batch"], local_batch)
-    trainer = Trainer(cfg, micro_batch=micro, device=device)
+    trainer = Trainer(cfg, micro_batch=micro, device=device, bucket_cap_mb=args.bucket_mb)
     ids, labels = next_token_batch(local_batch, SEQ, seed=1000 + rank, device=device)
 
     def barrier():
@@ -252,6 +266,8 @@ def main(argv: list[str] | None = None) -> int:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    if args.phase_split:
+        trainer.phase_log = []
     with ClockSampler(local) as clocks:
         clocks.mark()
         start.record(stream)
@@ -267,6 +283,20 @@ def main(argv: list[str] | None = None) -> int:
     barrier()
     launches = _lib.launches - launches0
     _lib.timer.enabled = False
+    phases = None
+    if trainer.phase_log is not None:
+        ph = Trainer.phase_summary(trainer.phase_log)
+        trainer.phase_log = None
+        names = sorted(ph)
+        vec = torch.tensor([ph[k] for k in names], device=device, dtype=torch.float64)
+        if world > 1:
+            allv = [torch.empty_like(vec) for _ in range(world)]
+            dist.all_gather(allv, vec)
+        else:
+            allv = [vec]
+        per_rank = torch.stack(allv).cpu()
+        phases = {k: {"min_over_ranks": float(per_rank[:, i].min()), "max_over_ranks": float(per_rank[:, i].max())}
+                  for i, k in enumerate(names)}
     kern = _lib.timer.summary()
     elapsed = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
     if world > 1:
@@ -365,6 +395,9 @@ def main(argv: list[str] | None = None) -> int:
                 "architecture": wl["model"] + " (dropout 0, tied embeddings)",
                 "global_batch": GLOBAL_BATCH, "seq_len": SEQ, "micro_batch": micro,
                 "grad_accum": math.ceil(local_batch / micro), "parallelism": f"dp{world}",
+                "allreduce": f"NCCL, fp32 gradients, {args.bucket_mb} MB buckets overlapped with backward, "
+                             f"{args.comm_priority}-priority stream"
+                             + (f", at most {args.comm_max_ctas} CTAs" if args.comm_max_ctas else ""),
                 "optimizer": "fused AdamW, fp32 master weights",
                 "l2": f"no flush: per-step working set (activations of {micro} x {SEQ} tokens, tens of GB) "
                       "is far larger than L2",
@@ -388,6 +421,7 @@ def main(argv: list[str] | None = None) -> int:
                     "note": "per rank: pinned host tokens copied to HBM and the loss read back every step",
                     "step_ms": spread(e2e_ev)},
             "step_ms": spread(step_ev),
+            **({"phase_ms": phases} if phases is not None else {}),
             "gpu_launches": launches,
             "peak_memory_gb": torch.cuda.max_memory_allocated(device) / 1e9,
             "device_status": status,

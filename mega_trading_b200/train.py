@@ -25,9 +25,16 @@ from .model import ModelConfig, TradingModelB200
 from .optim import AdamWShadow
 
 
-def init_distributed(backend: str = "nccl", timeout_s: int = 300) -> tuple[int, int, int]:
+def init_distributed(backend: str = "nccl", timeout_s: int = 300, *, comm_high_priority: bool = True,
+                     comm_max_ctas: int | None = None) -> tuple[int, int, int]:
     """Initialise the default process group from torchrun's environment; returns
-    ``(rank, world_size, local_rank)`` (``(0, 1, 0)`` without torchrun)."""
+    ``(rank, world_size, local_rank)`` (``(0, 1, 0)`` without torchrun).
+
+    With NCCL the gradient all-reduce runs on a high-priority stream by default:
+    the step's persistent kernels hold every SM, and when their CTAs retire the
+    block scheduler then places the waiting all-reduce CTAs before the next
+    compute kernel's, so the collective keeps pace with the backward instead of
+    piling up behind it.  ``comm_max_ctas`` caps the SMs NCCL takes per collective."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world <= 1:
         return 0, 1, 0
@@ -39,6 +46,11 @@ def init_distributed(backend: str = "nccl", timeout_s: int = 300) -> tuple[int, 
         kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
         if backend == "nccl":
             kwargs["device_id"] = torch.device("cuda", local)
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = bool(comm_high_priority)
+            if comm_max_ctas:
+                opts.config.max_ctas = int(comm_max_ctas)
+            kwargs["pg_options"] = opts
         dist.init_process_group(backend=backend, **kwargs)
     return rank, world, local
 
@@ -79,6 +91,16 @@ class Trainer:
         # AdamW leaves the weights alone when it is set, and every step polls it
         # without stalling (an error raises at most two steps later)
         self.monitor = _lib.StatusMonitor(device) if device.type == "cuda" else None
+        # analysis hook: a list here collects, per step, CUDA event pairs around the
+        # forward, backward (the last one includes waiting for the gradient
+        # all-reduce) and optimizer phases on the current stream
+        self.phase_log: list | None = None
+
+    def _mark(self, marks: list | None, name: str) -> None:
+        if marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
 
     def check_status(self) -> None:
         """Wait for the device and raise :class:`~mega_trading_b200._lib.B200KernelError` if a
@@ -93,6 +115,8 @@ class Trainer:
         n = input_ids.shape[0]
         chunks = max(1, (n + self.micro_batch - 1) // self.micro_batch)
         total = torch.zeros((), device=input_ids.device, dtype=torch.float32)
+        marks = [] if (self.phase_log is not None and input_ids.is_cuda) else None
+        self._mark(marks, "start")
         for i in range(chunks):
             lo = i * self.micro_batch
             hi = min(n, lo + self.micro_batch)
@@ -100,10 +124,24 @@ class Trainer:
             sync_ctx = self.engine.no_sync() if (self.world > 1 and i < chunks - 1) else contextlib.nullcontext()
             with sync_ctx:
                 loss = self.engine(input_ids[lo:hi], labels[lo:hi])
+                self._mark(marks, "forward")
                 (loss * frac).backward()
+                self._mark(marks, "backward" if i < chunks - 1 else "backward+allreduce")
             total += loss.detach() * frac
         self.opt.step()
         self.opt.zero_grad(set_to_none=self.world == 1)
+        self._mark(marks, "optimizer")
+        if marks is not None:
+            self.phase_log.append(marks)
         if self.monitor is not None:
             self.monitor.poll()
         return total
+
+    @staticmethod
+    def phase_summary(log: list) -> dict:
+        """Mean milliseconds per phase over the steps in ``log`` (events must have completed)."""
+        acc: dict[str, float] = {}
+        for marks in log:
+            for (_, a), (name, b) in zip(marks, marks[1:]):
+                acc[name] = acc.get(name, 0.0) + a.elapsed_time(b)
+        return {k: v / max(len(log), 1) for k, v in acc.items()}
