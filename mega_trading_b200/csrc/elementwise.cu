@@ -10,6 +10,8 @@
 // B200 design: pure HBM streaming.  Each thread moves 16 bytes per tensor per
 // step (8 bf16/fp16 elements = 4 RoPE pairs), math in fp32 with one rounding
 // per output, grid-stride loops sized to a multiple of the SM count.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace mt {
@@ -19,12 +21,21 @@ constexpr int kThreads = 256;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int grid_for(int64_t units) {
-  const int64_t per_wave = int64_t(get_sm_count()) * 8;  // 8 blocks of 256 threads per SM
+// Blocks for `units` one-per-thread work items, at most `max_waves` full waves
+// (8 blocks of 256 threads per SM) with grid-stride loops beyond that.
+// Measured side by side on the config-2 shapes (65,536 x 2048): the packed
+// SwiGLU kernels and the plain backward run 6-7 % faster with one item per
+// thread than with a 4-wave grid, the plain forward 12 % slower (it keeps 4
+// waves); RoPE is within 1 % either way (8 waves).
+int grid_for(int64_t units, int64_t max_waves) {
+  const int64_t per_wave = int64_t(get_sm_count()) * 8;
   int64_t blocks = (units + kThreads - 1) / kThreads;
-  if (blocks > per_wave * 4) blocks = per_wave * 4;
+  blocks = std::min<int64_t>(blocks, std::min<int64_t>(per_wave * max_waves, int64_t(1) << 30));
   return (int)(blocks < 1 ? 1 : blocks);
 }
+constexpr int64_t kRopeWaves = 8;
+constexpr int64_t kSwigluWaves = int64_t(1) << 20;
+constexpr int64_t kSwigluFwdWaves = 4;
 
 template <typename F>
 int with_half_dtype(int code, F&& f) {
@@ -301,13 +312,13 @@ int mt_rope(const void* q, const void* k, const void* cos, const void* sin, void
       const bool head_inner = qs[1] < qs[2] && ks[1] < ks[2] && qos[1] < qos[2] && kos[1] < kos[2];
       if constexpr (sizeof(TT) == 2) {
         if (head_inner)
-          rope_vec<TT, true><<<grid_for(ut), kThreads, 0, s>>>(a, dv, (uint32_t)uq, (uint32_t)ut);
+          rope_vec<TT, true><<<grid_for(ut, kRopeWaves), kThreads, 0, s>>>(a, dv, (uint32_t)uq, (uint32_t)ut);
         else
-          rope_vec<TT, false><<<grid_for(ut), kThreads, 0, s>>>(a, dv, (uint32_t)uq, (uint32_t)ut);
+          rope_vec<TT, false><<<grid_for(ut, kRopeWaves), kThreads, 0, s>>>(a, dv, (uint32_t)uq, (uint32_t)ut);
       }
     } else {
       const int64_t uq = rows_q * (D / 2), ut = uq + rows_k * (D / 2);
-      rope_scalar<TT><<<grid_for(ut), kThreads, 0, s>>>(a, uq, ut);
+      rope_scalar<TT><<<grid_for(ut, kRopeWaves), kThreads, 0, s>>>(a, uq, ut);
     }
     return check_launch("rope");
   });
@@ -321,7 +332,7 @@ int mt_swiglu_fwd(const void* g, const void* u, void* y, int dtype, int64_t n, v
   return with_half_dtype(dtype, [&](auto tv) {
     using TT = decltype(tv);
     const int64_t vecs = n / (16 / (int64_t)sizeof(TT)) + 1;
-    swiglu_fwd_k<TT><<<grid_for(vecs), kThreads, 0, s>>>(static_cast<const TT*>(g), static_cast<const TT*>(u),
+    swiglu_fwd_k<TT><<<grid_for(vecs, kSwigluFwdWaves), kThreads, 0, s>>>(static_cast<const TT*>(g), static_cast<const TT*>(u),
                                                           static_cast<TT*>(y), n);
     return check_launch("swiglu_fwd");
   });
@@ -337,7 +348,7 @@ int mt_swiglu_bwd(const void* g, const void* u, const void* dy, void* dg, void* 
   return with_half_dtype(dtype, [&](auto tv) {
     using TT = decltype(tv);
     const int64_t vecs = n / (16 / (int64_t)sizeof(TT)) + 1;
-    swiglu_bwd_k<TT><<<grid_for(vecs), kThreads, 0, s>>>(static_cast<const TT*>(g), static_cast<const TT*>(u),
+    swiglu_bwd_k<TT><<<grid_for(vecs, kSwigluWaves), kThreads, 0, s>>>(static_cast<const TT*>(g), static_cast<const TT*>(u),
                                                           static_cast<const TT*>(dy), static_cast<TT*>(dg),
                                                           static_cast<TT*>(du), n);
     return check_launch("swiglu_bwd");
@@ -357,7 +368,7 @@ int mt_swiglu_packed_fwd(const void* gu, void* y, int dtype, int64_t rows, int64
     if constexpr (sizeof(TT) == 2) {
       FastDiv vpr;
       vpr.init((uint32_t)(inter / 8));
-      swiglu_packed_fwd_k<TT><<<grid_for(rows * inter / 8), kThreads, 0, s>>>(
+      swiglu_packed_fwd_k<TT><<<grid_for(rows * inter / 8, kSwigluWaves), kThreads, 0, s>>>(
           static_cast<const TT*>(gu), static_cast<TT*>(y), (uint32_t)(rows * inter / 8), vpr, (int)inter);
     }
     return check_launch("swiglu_packed_fwd");
@@ -377,7 +388,7 @@ int mt_swiglu_packed_bwd(const void* gu, const void* dy, void* dgu, int dtype, i
     if constexpr (sizeof(TT) == 2) {
       FastDiv vpr;
       vpr.init((uint32_t)(inter / 8));
-      swiglu_packed_bwd_k<TT><<<grid_for(rows * inter / 8), kThreads, 0, s>>>(
+      swiglu_packed_bwd_k<TT><<<grid_for(rows * inter / 8, kSwigluWaves), kThreads, 0, s>>>(
           static_cast<const TT*>(gu), static_cast<const TT*>(dy), static_cast<TT*>(dgu), (uint32_t)(rows * inter / 8),
           vpr, (int)inter);
     }
