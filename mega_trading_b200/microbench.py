@@ -420,6 +420,34 @@ def reference_cases(dev, iters, seqs=(1024, 2048, 4096), n=65536):
             out.append({"op": "ref_attention_bwd", "T": T, "oom": str(exc).splitlines()[0][:160]})
         del q, k, v, do
         torch.cuda.empty_cache()
+    # the one shape the reference runs a Triton attention backward on
+    # (kernels/triton_attention.py:114-131: T=512, Hq 16 / Hkv 4, D 64, bf16), ours beside it
+    B, Hq, Hkv, D, T = 64, 16, 4, 64, 512
+    g = torch.Generator(device=dev).manual_seed(512)
+    q = (torch.randn(B, Hq, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+    k = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+    v = (torch.randn(B, Hkv, T, D, device=dev, generator=g) * 0.5).bfloat16().requires_grad_(True)
+    do = torch.randn(B, Hq, T, D, device=dev, generator=g).bfloat16()
+    flops = 4.0 * B * Hq * D * T * (T + 1) / 2
+    mf = timed("ref_attention_fwd", lambda: RA.triton_attention(q, k, v, repeats=Hq // Hkv), T=T, B=B)
+    if mf:
+        out[-1]["tflops"] = flops / mf / 1e9
+    o = RA.triton_attention(q, k, v, repeats=Hq // Hkv)
+    mb = timed("ref_attention_bwd", lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True), T=T, B=B)
+    if mb:
+        out[-1]["tflops"] = 2.5 * flops / mb / 1e9
+    del o
+    qd, kd, vd = q.detach(), k.detach(), v.detach()
+    scale = 1.0 / math.sqrt(D)
+    o, lse = A._launch_fwd(qd, kd, vd, Hq // Hkv, scale)
+    mf = timed("attention_fwd", lambda: A._launch_fwd(qd, kd, vd, Hq // Hkv, scale), T=T, B=B)
+    if mf:
+        out[-1]["tflops"] = flops / mf / 1e9
+    mb = timed("attention_bwd", lambda: A._launch_bwd(qd, kd, vd, o, lse, do, scale), T=T, B=B)
+    if mb:
+        out[-1]["tflops"] = 2.5 * flops / mb / 1e9
+    del q, k, v, do, o, lse, qd, kd, vd
+    torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(9)
     H, I, V = 768, 2048, 21504
     bf = torch.bfloat16
