@@ -8,8 +8,9 @@ master weights and fused AdamW -- on seeded synthetic composite-token streams
 already resident in HBM.  ``--model large24`` runs BASELINE config 4 instead
 (24 layers, d_model 1024, 16/4 GQA heads, SwiGLU 2816, seq 4096, global batch
 128).  One JSON line on rank 0 (see the contract fields below).
-``--impl reference`` times the reference's own PyTorch path (the CPU fp32
-restatement in ``oracle/``) on the host cores instead.
+``--impl reference`` times the reference's own PyTorch train step on the host
+cores instead: its ``TradingModel`` from the copy installed under
+``baseline/_ref`` when present, else the CPU fp32 restatement in ``oracle/``.
 """
 
 from __future__ import annotations
@@ -132,25 +133,53 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, budget_s: float = 12.0,
-                           model_name: str = "gqa12") -> dict:
-    """The reference's PyTorch train step (oracle/ CPU fp32 restatement) on the host cores."""
+def _cpu_trainer(model_name: str):
+    """The CPU fp32 train step the CPU legs time: the reference's own ``TradingModel`` from the
+    installed copy under ``baseline/_ref`` (its torch operator path, ``attention_backend="auto"``,
+    dropout 0) when that copy is present (kind ``reference``), else the oracle's restatement
+    (kind ``port``).  Both step forward_with_loss, backward and AdamW with the reference's
+    settings (lr 2e-4, betas (0.9, 0.999), eps 1e-8, weight decay 0.01)."""
+    from dataclasses import asdict
+
     from oracle.model import TradingModelRef, make_optimizer, train_step
 
+    from mega_trading_b200.microbench import load_reference
+    from mega_trading_b200.model import CONFIGS
+
+    torch.manual_seed(0)
+    ref = load_reference()
+    if ref is not None:
+        model = ref[2].TradingModel(dropout=0.0, attention_backend="auto", **asdict(CONFIGS[model_name]))
+        opt = make_optimizer(model)
+
+        def step(ids, labels):
+            loss, _ = model.forward_with_loss(ids, labels, return_logits=False)
+            loss.backward()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            return loss.detach()
+
+        return step, "reference", "the reference's own TradingModel (baseline/_ref), torch operator path"
+    model = TradingModelRef(_ref_config(model_name))
+    opt = make_optimizer(model)
+    return (lambda ids, labels: train_step(model, opt, ids, labels)), "port", "oracle restatement of the reference"
+
+
+def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, budget_s: float = 12.0,
+                           model_name: str = "gqa12") -> dict:
+    """The reference's PyTorch train step on the host cores (see ``_cpu_trainer``)."""
     from mega_trading_b200.data import next_token_batch
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    torch.manual_seed(0)
-    model = TradingModelRef(_ref_config(model_name))
-    opt = make_optimizer(model)
+    train_step, kind, what = _cpu_trainer(model_name)
     ids, labels = next_token_batch(seqs, seq_len, seed=7, device="cpu")
-    train_step(model, opt, ids, labels)  # warm-up
+    train_step(ids, labels)  # warm-up
     times = []
     t_start = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        train_step(model, opt, ids, labels)
+        train_step(ids, labels)
         times.append(time.perf_counter() - t0)
         if steps is not None and len(times) >= steps:
             break
@@ -158,9 +187,9 @@ def cpu_train_tokens_per_s(seqs: int, seq_len: int, steps: int | None = None, bu
             break
     tok = seqs * seq_len
     return {"value": tok / statistics.mean(times), "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "port", "steps": len(times),
+            "kind": kind, "steps": len(times),
             "sample": f"{seqs} x {seq_len}-token sequence(s) per step of the {WORKLOADS[model_name]['model']} "
-                      "model, fp32, full step "
+                      f"model ({what}), fp32, full step "
                       f"(forward, CE, backward, AdamW); {len(times)} timed step(s)"}
 
 
@@ -171,20 +200,16 @@ def run_reference(args) -> None:
     steps, warm = args.steps, args.warmup
     wl = WORKLOADS[args.model]
     SEQ = wl["seq"]
-    from oracle.model import TradingModelRef, make_optimizer, train_step
-
     from mega_trading_b200.data import next_token_batch
 
     torch.set_num_threads(os.cpu_count() or 1)
-    torch.manual_seed(0)
-    model = TradingModelRef(_ref_config(args.model))
-    opt = make_optimizer(model)
+    train_step, kind, what = _cpu_trainer(args.model)
     ids, labels = next_token_batch(CPU_SAMPLE_SEQS, SEQ, seed=7, device="cpu")
     for _ in range(warm):
-        train_step(model, opt, ids, labels)
+        train_step(ids, labels)
     t0 = time.perf_counter()
     for _ in range(steps):
-        train_step(model, opt, ids, labels)
+        train_step(ids, labels)
     el = time.perf_counter() - t0
     tok = CPU_SAMPLE_SEQS * SEQ
     value = tok * steps / el
@@ -194,9 +219,10 @@ def run_reference(args) -> None:
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic composite-token streams",
         "config": {"workload": wl["workload"], "architecture": wl["model"],
                    "global_batch": CPU_SAMPLE_SEQS, "seq_len": SEQ, "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": kind,
                          "sample": f"{CPU_SAMPLE_SEQS} x {SEQ}-token sequence per step (bounded sample of the "
-                                   f"global batch of {wl['global_batch']}), fp32 forward+CE+backward+AdamW"},
+                                   f"global batch of {wl['global_batch']}) through {what}, "
+                                   "fp32 forward+CE+backward+AdamW"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
