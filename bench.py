@@ -287,7 +287,7 @@ def main(argv: list[str] | None = None) -> int:
     # ---------------- timed region: K steps, inputs resident in HBM ----------------
     _lib.timer.reset()
     _lib.timer.enabled = True
-    launches0 = _lib.launches
+    launches0 = _lib.launch_count()
     stream = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -307,7 +307,7 @@ def main(argv: list[str] | None = None) -> int:
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
-    launches = _lib.launches - launches0
+    launches = _lib.launch_count() - launches0
     _lib.timer.enabled = False
     phases = None
     if trainer.phase_log is not None:

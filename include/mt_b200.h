@@ -81,6 +81,12 @@ MT_API int mt_debug_wait_timeout(int64_t limit_cycles, int complete, uint32_t* s
  * that kernel alone inside a multi-kernel operator.  Both NULL disables it. */
 MT_API int mt_set_timing_events(void* before_main, void* after_main);
 
+/* Launch counter (no counterpart in the reference): the number of kernels this
+ * library has launched successfully in the process so far, over all devices
+ * and host threads.  A caller takes the difference around a region to count
+ * the library's kernels in it. */
+MT_API int64_t mt_launch_count(void);
+
 /* ---------------------------------------------------------------------
  * RMSNorm   replaces triton_rms_norm (src/mega_trading/kernels/triton_ops.py:11-15,
  *           forward kernel :528-538, backward :633-665 + torch sum :183)

@@ -58,6 +58,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "mt_swiglu_gemm_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "mt_qkv_rope_gemm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                  c_vp, c_vp]),
+    "mt_launch_count": (c_i64, []),
     "mt_set_timing_events": (c_int, [c_vp, c_vp]),
     "mt_rope": (
         c_int,
@@ -253,14 +254,10 @@ def require_cuda_sm100(t: torch.Tensor, op: str) -> None:
         raise RuntimeError(f"{op} requires an sm_100 (B200) GPU, found sm_{major}{minor}")
 
 
-# Launch counter: every successful C-ABI compute call increments it by the
-# number of kernels it launched (used by bench.py to report gpu_launches).
-launches = 0
-
-
-def count(n: int) -> None:
-    global launches
-    launches += n
+def launch_count() -> int:
+    """Kernels the library has launched in this process (its own counter,
+    ``mt_launch_count``); bench.py reports the difference over the timed region."""
+    return int(load().mt_launch_count())
 
 
 class KernelTimer:

@@ -1,6 +1,7 @@
 // Library-wide C-ABI helpers: status strings, error capture, device checks,
 // tensor-map encoding through the runtime's driver entry point (so the library
 // does not link libcuda directly and loads on hosts without a driver).
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -19,12 +20,17 @@ void set_last_error(const char* where, cudaError_t err) {
 
 void set_last_error_text(const char* text) { snprintf(g_last_error, sizeof(g_last_error), "%s", text); }
 
+// Kernels this library has launched in the process (every launch is followed
+// by exactly one check_launch).
+std::atomic<long long> g_launches{0};
+
 int check_launch(const char* where) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
     set_last_error(where, err);
     return MT_ERR_LAUNCH;
   }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return MT_OK;
 }
 
@@ -205,6 +211,7 @@ const char* mt_status_string(int status) {
 int mt_version(void) { return 1; }
 int mt_built_arch(void) { return 100; }
 const char* mt_last_error(void) { return mt::g_last_error; }
+int64_t mt_launch_count(void) { return mt::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"
 

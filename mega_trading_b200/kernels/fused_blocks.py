@@ -104,7 +104,6 @@ def _qkv_rope_gemm(x2, w, cos2, sin2, seq, rot_cols, head_dim):
                               cos2.stride(0), _lib.dtype_code(x2.dtype), m, hidden, n, rot_cols, seq, head_dim,
                               status.data_ptr(), _lib.stream_ptr(x2.device))
     _lib.check(st, "qkv_rope_gemm")
-    _lib.count(1)
     return qkv
 
 
@@ -162,7 +161,6 @@ class _SwiGLUPacked(torch.autograd.Function):
         st = lib.mt_swiglu_packed_fwd(gu.data_ptr(), y.data_ptr(), _lib.dtype_code(gu.dtype), rows, inter,
                                       _lib.stream_ptr(gu.device))
         _lib.check(st, "swiglu_packed forward")
-        _lib.count(1)
         ctx.save_for_backward(gu)
         return y
 
@@ -177,7 +175,6 @@ class _SwiGLUPacked(torch.autograd.Function):
         st = lib.mt_swiglu_packed_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), _lib.dtype_code(gu.dtype), rows,
                                       inter, _lib.stream_ptr(gu.device))
         _lib.check(st, "swiglu_packed backward")
-        _lib.count(1)
         return dgu
 
 
@@ -219,7 +216,6 @@ class _SwiGLUMLP(torch.autograd.Function):
                                     _lib.dtype_code(x.dtype), m, hidden, inter, status.data_ptr(),
                                     _lib.stream_ptr(x.device))
         _lib.check(st, "swiglu_gemm forward")
-        _lib.count(1)
         out = torch.nn.functional.linear(y, w2)
         ctx.save_for_backward(x2, w13, w2, gu, y)
         return out.view(*x.shape[:-1], w2.shape[0])
@@ -239,7 +235,6 @@ class _SwiGLUMLP(torch.autograd.Function):
                                     _lib.dtype_code(gu.dtype), gu.shape[0], w2.shape[0], inter, status.data_ptr(),
                                     _lib.stream_ptr(gu.device))
         _lib.check(st, "swiglu_gemm backward")
-        _lib.count(1)
         dx = dgu.mm(w13)
         dw13 = dgu.t().mm(x2)
         return dx.view(*dout.shape[:-1], hidden), dw13, dw2

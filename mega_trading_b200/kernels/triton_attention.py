@@ -39,7 +39,6 @@ def _launch_fwd(q, k, v, repeats: int, scale: float):
     )
     _lib.timer.stop(tok)
     _lib.check(st, "attention forward")
-    _lib.count(1)
     return o, lse
 
 
@@ -73,7 +72,6 @@ def _launch_bwd(q, k, v, o, lse, do, scale: float, dq=None, dk=None, dv=None, ro
         st = lib.mt_attention_rope_bwd(*common, cos.data_ptr(), sin.data_ptr(), cos.stride(0), *tail)
     _lib.timer.stop(tok)
     _lib.check(st, "attention backward")
-    _lib.count(3)
     return dq, dk, dv
 
 

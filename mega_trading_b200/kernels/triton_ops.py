@@ -52,7 +52,6 @@ def _rms_fwd(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtyp
         _lib.dtype_code(out_dtype), rstd.data_ptr(), rows, dim, float(eps), _dev_stream(x),
     )
     _lib.check(st, "rms_norm forward")
-    _lib.count(1)
     return y, rstd
 
 
@@ -92,7 +91,6 @@ def _rms_bwd(x, w, rstd, dy, dx_dtype, residual_grad=None, branch_dtype=None):
             ws.data_ptr(), ws.numel(), rows, dim, _dev_stream(x),
         )
         _lib.check(st, "add_rms_norm backward (dual)")
-    _lib.count(2)
     if branch_dtype is not None:
         return dx, dw, (dx if dx2 is None else dx2)
     return dx, dw
@@ -149,7 +147,6 @@ class _AddRMSNorm(torch.autograd.Function):
             rstd.data_ptr(), rows, dim, float(eps), _dev_stream(x),
         )
         _lib.check(st, "add_rms_norm forward")
-        _lib.count(1)
         ctx.save_for_backward(new_res, w, rstd)
         ctx.hidden_dtype = hidden.dtype
         return new_res.view(residual.shape), normed.view(hidden.shape)
@@ -219,7 +216,6 @@ def _launch_rope(query, key, cos2, sin2, q_out, k_out, negate: bool) -> None:
         1 if negate else 0, _dev_stream(query),
     )
     _lib.check(st, "rope")
-    _lib.count(1)
 
 
 class _RoPE(torch.autograd.Function):
@@ -272,7 +268,6 @@ class _SwiGLUGate(torch.autograd.Function):
         st = lib.mt_swiglu_fwd(g.data_ptr(), u.data_ptr(), y.data_ptr(), _lib.dtype_code(g.dtype), g.numel(),
                                _dev_stream(g))
         _lib.check(st, "swiglu forward")
-        _lib.count(1)
         ctx.save_for_backward(g, u)
         return y
 
@@ -286,7 +281,6 @@ class _SwiGLUGate(torch.autograd.Function):
         st = lib.mt_swiglu_bwd(g.data_ptr(), u.data_ptr(), dy.data_ptr(), dg.data_ptr(), du.data_ptr(),
                                _lib.dtype_code(g.dtype), g.numel(), _dev_stream(g))
         _lib.check(st, "swiglu backward")
-        _lib.count(1)
         return dg, du
 
 

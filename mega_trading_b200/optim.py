@@ -251,4 +251,3 @@ class AdamWShadow(torch.optim.Optimizer):
                                float(beta1), float(beta2), float(eps), float(wd), float(lr / bc1),
                                float(math.sqrt(bc2)), _lib.status_word(dev).data_ptr(), _lib.stream_ptr(dev))
         _lib.check(st, "adamw step")
-        _lib.count(1)

@@ -22,7 +22,7 @@ def test_header_declares_the_hot_path():
     names = _declared()
     for n in ("mt_rms_norm_fwd", "mt_rms_norm_bwd", "mt_add_rms_norm_fwd", "mt_add_rms_norm_bwd", "mt_rope",
               "mt_swiglu_fwd", "mt_swiglu_bwd", "mt_attention_fwd", "mt_attention_bwd", "mt_fused_ce_fwd",
-              "mt_fused_ce_bwd", "mt_debug_wait_timeout"):
+              "mt_fused_ce_bwd", "mt_debug_wait_timeout", "mt_launch_count"):
         assert n in names
 
 
@@ -36,6 +36,7 @@ def test_library_exports_every_declared_symbol():
     assert lib.mt_built_arch() == 100
     assert lib.mt_status_string(0) == b"ok"
     assert lib.mt_status_string(6) == b"device-side wait timed out"
+    assert lib.mt_launch_count() >= 0
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
