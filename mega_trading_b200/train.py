@@ -16,6 +16,7 @@ from __future__ import annotations
 import contextlib
 import datetime
 import os
+import time
 
 import torch
 import torch.distributed as dist
@@ -55,12 +56,24 @@ def init_distributed(backend: str = "nccl", timeout_s: int = 300, *, comm_high_p
     return rank, world, local
 
 
+class PeerLostError(RuntimeError):
+    """A peer rank did not reach the start of this step within the peer timeout."""
+
+
 class Trainer:
-    """Owns the model replica, the DDP wrapper and the optimizer of one rank."""
+    """Owns the model replica, the DDP wrapper and the optimizer of one rank.
+
+    ``peer_timeout_s`` (multi-rank only) turns on a host-side liveness check at
+    the start of every step: each rank posts a heartbeat for the step in the
+    process group's store and waits, at most that long, for every peer's.  A
+    rank that has exited or stopped between steps makes the others raise
+    :class:`PeerLostError` before they launch any kernel or collective of the
+    step, so no device work ever waits on a missing peer.  Without it a lost
+    peer surfaces as the process group's timeout on the next all-reduce."""
 
     def __init__(self, cfg: ModelConfig, *, micro_batch: int, device: torch.device, lr: float = 2e-4,
                  weight_decay: float = 0.01, seed: int = 0, bucket_cap_mb: int = 64,
-                 model: torch.nn.Module | None = None) -> None:
+                 model: torch.nn.Module | None = None, peer_timeout_s: float | None = None) -> None:
         torch.manual_seed(seed)  # identical initial replicas on every rank
         self.cfg = cfg
         self.device = device
@@ -95,6 +108,31 @@ class Trainer:
         # forward, backward (the last one includes waiting for the gradient
         # all-reduce) and optimizer phases on the current stream
         self.phase_log: list | None = None
+        self.peer_timeout_s = peer_timeout_s if self.world > 1 else None
+        self._store = dist.distributed_c10d._get_default_store() if self.peer_timeout_s else None
+        self._steps = 0
+
+    def _await_peers(self) -> None:
+        """Post this rank's heartbeat for the coming step and wait for every peer's."""
+        n, me = self._steps, dist.get_rank()
+        self._store.set(f"mt_hb/{n}/{me}", "1")
+        if n >= 2:
+            self._store.delete_key(f"mt_hb/{n - 2}/{me}")
+        peers = [f"mt_hb/{n}/{r}" for r in range(self.world) if r != me]
+        t0 = time.monotonic()
+        try:
+            self._store.wait(peers, datetime.timedelta(seconds=float(self.peer_timeout_s)))
+        except Exception as exc:  # the store raises its own timeout / connection errors
+            missing = [k.rsplit("/", 1)[1] for k in peers if not self._safe_check(k)]
+            raise PeerLostError(
+                f"rank {me}: rank(s) {', '.join(missing) or '?'} did not reach step {n} within "
+                f"{time.monotonic() - t0:.1f} s ({type(exc).__name__}: {exc})") from exc
+
+    def _safe_check(self, key: str) -> bool:
+        try:
+            return bool(self._store.check([key]))
+        except Exception:
+            return False
 
     def _mark(self, marks: list | None, name: str) -> None:
         if marks is not None:
@@ -112,6 +150,9 @@ class Trainer:
     def step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         """One optimizer step over this rank's ``[B, T]`` batch; returns the mean loss (device scalar,
         no host synchronisation)."""
+        if self._store is not None:
+            self._await_peers()
+        self._steps += 1
         n = input_ids.shape[0]
         chunks = max(1, (n + self.micro_batch - 1) // self.micro_batch)
         total = torch.zeros((), device=input_ids.device, dtype=torch.float32)

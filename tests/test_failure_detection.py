@@ -39,7 +39,7 @@ class _LossWrapper(torch.nn.Module):
         return self.m.forward_with_loss(ids, labels)[0]
 
 
-def _worker(rank, world, port, mode, outdir):
+def _worker(rank, world, port, mode, outdir, peer_timeout_s=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from oracle.model import TradingModelRef
@@ -49,7 +49,7 @@ def _worker(rank, world, port, mode, outdir):
     init_distributed("gloo", timeout_s=PG_TIMEOUT_S)
     torch.manual_seed(0)
     tr = Trainer(_cfg(), micro_batch=2, device=torch.device("cpu"), model=_LossWrapper(TradingModelRef(_cfg())),
-                 seed=0)
+                 seed=0, peer_timeout_s=peer_timeout_s)
     g = torch.Generator().manual_seed(rank)
     ids = torch.randint(0, 64, (2, 16), generator=g)
     labels = torch.randint(0, 64, (2, 16), generator=g)
@@ -60,11 +60,12 @@ def _worker(rank, world, port, mode, outdir):
         time.sleep(PG_TIMEOUT_S * 4)  # alive, but never joins step 2
         os._exit(0)
     t0 = time.monotonic()
-    outcome = {"raised": None, "elapsed_s": None}
+    outcome = {"raised": None, "elapsed_s": None, "message": None}
     try:
         tr.step(ids, labels)
     except Exception as exc:  # noqa: BLE001 - the error type is backend specific
         outcome["raised"] = type(exc).__name__
+        outcome["message"] = str(exc)[:300]
     outcome["elapsed_s"] = time.monotonic() - t0
     with open(os.path.join(outdir, "rank0.json"), "w") as f:
         json.dump(outcome, f)
@@ -97,3 +98,28 @@ def test_peer_leaving_between_steps_fails_the_next_collective(tmp_path, mode):
     assert outcome["elapsed_s"] < PG_TIMEOUT_S * 3, outcome
     if dist.is_initialized():
         dist.destroy_process_group()
+
+
+HEARTBEAT_S = 2.0
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_peer_heartbeat_raises_before_the_collective(tmp_path, mode):
+    """With ``peer_timeout_s`` the surviving rank learns of the missing peer on the host, at the
+    start of its next step, and raises PeerLostError naming it before launching any work."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, str(tmp_path), HEARTBEAT_S)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert procs[0].exitcode == 0
+    outcome = json.loads((tmp_path / "rank0.json").read_text())
+    assert outcome["raised"] == "PeerLostError", outcome
+    assert "rank(s) 1" in outcome["message"], outcome
+    assert HEARTBEAT_S * 0.5 < outcome["elapsed_s"] < HEARTBEAT_S + PG_TIMEOUT_S, outcome
