@@ -9,6 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
+import time
 from pathlib import Path
 
 import torch
@@ -219,6 +220,7 @@ class StatusMonitor:
         self.device = device
         self.depth = max(1, int(depth))
         self.pending: list[tuple[torch.Tensor, torch.cuda.Event]] = []
+        self.blocked_s = 0.0  # host seconds spent waiting for the device in poll()
 
     def _inspect(self, host: torch.Tensor) -> None:
         v = int(host[0])
@@ -235,7 +237,9 @@ class StatusMonitor:
         self.pending.append((host, ev))
         while self.pending and (self.pending[0][1].query() or len(self.pending) > self.depth):
             h, e = self.pending.pop(0)
+            t0 = time.perf_counter()
             e.synchronize()
+            self.blocked_s += time.perf_counter() - t0
             self._inspect(h)
 
     def flush(self) -> None:
