@@ -245,6 +245,9 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--comm-priority", choices=("high", "normal"), default="high",
                     help="stream priority of the gradient all-reduce")
     ap.add_argument("--comm-max-ctas", type=int, default=None, help="cap on the CTAs NCCL uses per collective")
+    ap.add_argument("--host-profile", action="store_true",
+                    help="analysis: cProfile the host side of the timed steps and print the top entries and "
+                         "the host milliseconds per step to stderr")
     ap.add_argument("--phase-split", action="store_true",
                     help="also time the phases of each step (forward, backward, the last backward with the "
                          "gradient all-reduce, optimizer) with CUDA events on every rank")
@@ -298,14 +301,36 @@ def main(argv: list[str] | None = None) -> int:
         clocks.mark()
         start.record(stream)
         step_ev = []
+        prof = None
+        if args.host_profile:
+            import cProfile
+
+            prof = cProfile.Profile()
+            blocked0 = trainer.monitor.blocked_s
+            host_t0 = time.perf_counter()
+            prof.enable()
         for _ in range(args.steps):
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record(stream)
             loss = trainer.step(ids, labels)
             ev[1].record(stream)
             step_ev.append(ev)
+        if prof is not None:
+            prof.disable()
+            host_ms = 1000.0 * (time.perf_counter() - host_t0) / max(args.steps, 1)
         end.record(stream)
         torch.cuda.synchronize()
+        if prof is not None:
+            import io
+            import pstats
+
+            out = io.StringIO()
+            pstats.Stats(prof, stream=out).sort_stats("tottime").print_stats(15)
+            drain_ms = 1000.0 * (time.perf_counter() - host_t0) / max(args.steps, 1) - host_ms
+            print(f"rank {rank}: host {host_ms:.1f} ms per step (the device finished {drain_ms * args.steps:.1f} ms "
+                  f"after the host loop); status-monitor wait "
+                  f"{1000.0 * (trainer.monitor.blocked_s - blocked0) / max(args.steps, 1):.1f} ms per step\n"
+                  f"{out.getvalue()}", file=sys.stderr, flush=True)
     barrier()
     launches = _lib.launch_count() - launches0
     _lib.timer.enabled = False
