@@ -155,3 +155,37 @@ def test_fused_ce_validation_messages(cuda_device):
         K.triton_fused_linear_cross_entropy(h[None], w, torch.zeros(4, dtype=torch.long, device=cuda_device))
     with pytest.raises(ValueError, match="labels must be an integer tensor"):
         K.triton_fused_linear_cross_entropy(h, w, torch.zeros(4, device=cuda_device))
+
+
+def test_fused_ce_out_of_range_labels_set_the_status_word(cuda_device):
+    """A target outside [0, V) that is not ignore_index (torch's cross_entropy, the reference's
+    CPU path, rejects it) is turned by the kernels' own bounds check into a status code
+    ((3 << 16) | 0xEEEE) instead of an out-of-bounds read; the row contributes no loss and no
+    gradient, exactly like an ignored row."""
+    from mega_trading_b200 import _lib
+    from mega_trading_b200.kernels import triton_ops as K
+
+    g = torch.Generator().manual_seed(21)
+    hidden = (torch.randn(40, 64, generator=g) * 0.5).bfloat16()
+    weight = (torch.randn(50, 64, generator=g) * 0.02).bfloat16()
+    labels = torch.randint(0, 50, (40,), generator=g, dtype=torch.long)
+    labels[3], labels[7], labels[11] = 50, -5, -100
+    assert _lib.read_status(cuda_device) == 0
+    hd = hidden.to(cuda_device).requires_grad_(True)
+    wd = weight.to(cuda_device).requires_grad_(True)
+    loss = K.triton_fused_linear_cross_entropy(hd, wd, labels.to(cuda_device), ignore_index=-100)
+    loss.backward()
+    code = _lib.read_status(cuda_device)  # reads and clears
+    assert code == (3 << 16) | 0xEEEE, hex(code)
+    assert "out of range" in _lib.describe_status(code)
+    masked = labels.clone()
+    masked[3] = masked[7] = -100
+    ho = hidden.float().requires_grad_(True)
+    wo = weight.float().requires_grad_(True)
+    lo = O.linear_cross_entropy(ho, wo, masked, -100)
+    lo.backward()
+    rel = abs(float(loss.detach()) - float(lo.detach())) / abs(float(lo.detach()))
+    assert rel <= 1e-3, f"loss rel err {rel:.3e}"
+    assert bool((hd.grad[3] == 0).all()) and bool((hd.grad[7] == 0).all())
+    _check_grads(hd.grad, ho.grad, wd.grad, wo.grad)
+    assert _lib.read_status(cuda_device) == 0
