@@ -60,6 +60,8 @@ FWD_CASES = [
     (1, 8, 8, 129, 32, torch.bfloat16, 43, 1.0, "contiguous"),
     (3, 2, 1, 1, 64, torch.float16, 44, 1.0, "contiguous"),
     (1, 4, 1, 640, 64, torch.float16, 45, 2.0, "model"),
+    (1, 9, 3, 2047, 64, torch.bfloat16, 46, 1.0, "contiguous"),  # odd repeats, one short of 16 tiles
+    (1, 8, 1, 200, 32, torch.float16, 47, 1.0, "model"),         # repeats 8, D 32, model layout
 ]
 
 
@@ -93,6 +95,10 @@ BWD_CASES = [
     (1, 6, 2, 300, 64, torch.bfloat16, 52, 1.0, "contiguous"),
     (1, 8, 8, 129, 32, torch.bfloat16, 53, 1.0, "contiguous"),
     (3, 2, 1, 1, 64, torch.float16, 54, 1.0, "contiguous"),
+    (1, 4, 1, 640, 64, torch.float16, 55, 2.0, "model"),       # fp16, repeats 4, scaled inputs
+    (1, 9, 3, 257, 64, torch.bfloat16, 56, 1.0, "contiguous"),  # odd repeats, one past a tile
+    (1, 4, 2, 1000, 32, torch.bfloat16, 57, 1.0, "model"),      # D 32 at a longer ragged T
+    (1, 8, 1, 200, 64, torch.bfloat16, 58, 1.0, "contiguous"),  # repeats 8 (one kv head)
 ]
 
 
