@@ -38,7 +38,8 @@ def _oracle_leaf(t, dtype):
 
 @pytest.mark.parametrize("shape,dtype,seed", [((2, 512, 1024), torch.bfloat16, 19), ((4, 77, 768), torch.bfloat16, 3),
                                               ((3, 5, 200), torch.float16, 4), ((64, 768), torch.float32, 5),
-                                              ((1, 1, 4096), torch.bfloat16, 6), ((2, 3, 12), torch.bfloat16, 7)])
+                                              ((1, 1, 4096), torch.bfloat16, 6), ((2, 3, 12), torch.bfloat16, 7),
+                                              ((2, 64, 1536), torch.bfloat16, 33), ((3, 2048), torch.float16, 34)])
 def test_rms_norm_matches_oracle(cuda_device, shape, dtype, seed):
     from mega_trading_b200.kernels import triton_ops as K
 
@@ -105,7 +106,8 @@ def test_add_rms_norm_mixed_dual_gradient(cuda_device, rows, dim):
 
 
 @pytest.mark.parametrize("shape,dtype,seed", [((2, 512, 1024), torch.bfloat16, 37), ((5, 33, 768), torch.float16, 8),
-                                              ((16, 768), torch.float32, 9)])
+                                              ((16, 768), torch.float32, 9), ((40, 1536), torch.bfloat16, 35),
+                                              ((7, 2048), torch.bfloat16, 36)])
 def test_add_rms_norm_matches_oracle(cuda_device, shape, dtype, seed):
     from mega_trading_b200.kernels import triton_ops as K
 
