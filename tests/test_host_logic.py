@@ -244,3 +244,29 @@ def test_bench_workloads_match_the_model_configs():
                       "rope_theta", "norm_eps", "block_size"):
             assert getattr(ref, field) == getattr(cfg, field), (name, field)
         assert cfg.block_size >= bench.WORKLOADS[name]["seq"]
+
+
+def test_bench_reference_arm_prints_the_contract_line(capsys, monkeypatch):
+    """``bench.py --impl reference`` on the host: one JSON line with the contract keys, the
+    reference arm's e2e without host-device copies, and a cpu_baseline naming what ran; a
+    non-zero rank prints nothing (only rank 0 runs the arm under torchrun)."""
+    import json
+
+    import bench
+
+    monkeypatch.setenv("RANK", "1")
+    assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "0"]) == 0
+    assert capsys.readouterr().out == ""
+    monkeypatch.setenv("RANK", "0")
+    assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "0"]) == 0
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["value"] > 0
+    assert d["metric"] == bench.WORKLOADS["gqa12"]["metric"]
+    assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["e2e"]["value"] == d["value"]
